@@ -1,0 +1,107 @@
+/*
+ * C ABI of the Blackwell (sm_100a) FlashAttention-2 forward.
+ *
+ * This is the drop-in boundary for the reference's hot path. In the reference
+ * (roy6n23/triton-fa2-forward) the Python wrapper `attention()` validates its inputs
+ * (fa2/kernel.py:218-244) and launches the Triton kernel `_attn_fwd[grid](...)` with
+ * q/k/v/out pointers, their 16 strides, (H_q, N_q, N_kv, qk_scale) and the constexprs
+ * GQA_GROUP / PACK / HEAD_DIM / CAUSAL (fa2/kernel.py:246-259). `fa2_fwd_sm100` takes
+ * the same information as plain pointers, sizes and strides and launches the CUDA kernel
+ * asynchronously on the caller's stream. No torch types cross this boundary.
+ *
+ * Layout: q and o are [B, H_q, N_q, D], k and v are [B, H_kv, N_kv, D], each with
+ * arbitrary element strides given in the order (b, h, n, d). The d stride must be 1,
+ * every other stride must be a multiple of 8 elements (16 bytes) and the base pointers
+ * must be 16-byte aligned (TMA rules); otherwise FA2_ERR_LAYOUT is returned and the
+ * caller should pass contiguous copies.
+ */
+#ifndef FA2_SM100_H_
+#define FA2_SM100_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA2_SM100_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FA2_API __attribute__((visibility("default")))
+#else
+#define FA2_API
+#endif
+
+enum Fa2DType { FA2_DTYPE_FP16 = 0, FA2_DTYPE_BF16 = 1 };
+
+enum Fa2Status {
+  FA2_OK = 0,
+  FA2_ERR_NULL = 1,          /* a required pointer is NULL */
+  FA2_ERR_SHAPE = 2,         /* non-positive size, batch mismatch, N_q != N_kv under causal */
+  FA2_ERR_DTYPE = 3,         /* dtype is neither fp16 nor bf16 */
+  FA2_ERR_HEAD_DIM = 4,      /* head_dim not supported by the compiled kernels */
+  FA2_ERR_GQA = 5,           /* H_q % H_kv != 0 */
+  FA2_ERR_PACK = 6,          /* pack_gqa requested but the group does not divide BLOCK_M (128) */
+  FA2_ERR_SCALE = 7,         /* qk_scale not finite or not > 0 */
+  FA2_ERR_LAYOUT = 8,        /* strides / alignment not usable by TMA */
+  FA2_ERR_TMA_ENCODE = 9,    /* cuTensorMapEncodeTiled rejected a descriptor */
+  FA2_ERR_LAUNCH = 10,       /* the CUDA launch failed (cudaGetLastError) */
+  FA2_ERR_DEVICE = 11,       /* current device is not sm_100 / driver entry point missing */
+  FA2_ERR_TIMEOUT = 12       /* value written to err_flag by a kernel whose bounded wait expired */
+};
+
+typedef struct Fa2FwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t q_stride[4]; /* element strides, order (b, h, n, d) */
+  int64_t k_stride[4];
+  int64_t v_stride[4];
+  int64_t o_stride[4];
+  int32_t batch;
+  int32_t heads_q;
+  int32_t heads_kv;
+  int32_t seqlen_q;
+  int32_t seqlen_kv;
+  int32_t head_dim;  /* 64 or 128 */
+  int32_t dtype;     /* Fa2DType */
+  int32_t causal;    /* top-left aligned causal mask; requires seqlen_q == seqlen_kv */
+  int32_t pack_gqa;  /* 1: a GQA group's query heads share one 128-row tile */
+  float qk_scale;    /* sm_scale * log2(e), > 0 (fa2/kernel.py:240-244) */
+  int32_t* err_flag; /* optional device int32; a kernel that gives up on a wait ORs
+                        FA2_ERR_TIMEOUT into it. NULL: no report. */
+  int64_t timeout_cycles; /* per-wait limit in SM clocks; <= 0 selects the default (~1 s) */
+} Fa2FwdParams;
+
+/* Host-only validation of `p` (no CUDA calls). Replaces the asserts and ValueErrors of
+ * fa2/kernel.py:218-244 at the C level. Returns FA2_OK or the first failing Fa2Status. */
+FA2_API int fa2_fwd_sm100_check(const Fa2FwdParams* p);
+
+/* out = softmax(q k^T * sm_scale [+ causal mask]) v, launched on `stream` (a
+ * cudaStream_t / CUstream; NULL = legacy default stream). Asynchronous: returns after
+ * the launch, without synchronising. Replaces `_attn_fwd[grid](...)`
+ * (fa2/kernel.py:246-259). */
+FA2_API int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream);
+
+/* Static description of the compiled kernel family (fa2/kernel.py:186-195 analogue):
+ * fills BLOCK_M, BLOCK_N, threads per CTA, K/V pipeline stages and dynamic shared memory
+ * bytes for `head_dim`. Returns FA2_OK or FA2_ERR_HEAD_DIM. Host only. */
+FA2_API int fa2_fwd_sm100_config(int32_t head_dim, int32_t* block_m, int32_t* block_n,
+                         int32_t* threads, int32_t* stages, int32_t* smem_bytes);
+
+/* Human-readable text for a Fa2Status. Never NULL. */
+FA2_API const char* fa2_sm100_strerror(int status);
+
+/* FA2_SM100_ABI_VERSION of the loaded library. */
+FA2_API int fa2_sm100_abi_version(void);
+
+/* sizeof(Fa2FwdParams) as compiled into the library, so a binding (ctypes, cgo, ...) can
+ * verify its mirror of the struct before the first call. */
+FA2_API int64_t fa2_sm100_params_size(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA2_SM100_H_ */

@@ -1,0 +1,691 @@
+// FlashAttention-2 forward for Blackwell (sm_100a): TMA + tcgen05 + TMEM, warp specialised.
+//
+// Reference path being replaced (roy6n23/triton-fa2-forward):
+//   fa2/kernel.py:110-183  _attn_fwd        (program = one Q tile of one (batch, q-head))
+//   fa2/kernel.py:60-107   _attn_fwd_inner  (per K/V tile: S = QK^T, mask, online softmax, PV)
+//   fa2/kernel.py:210-260  attention()      (validation, pack decision, launch)
+//
+// One CTA owns two Q tiles of 128 rows (256 rows; with GQA packing a row is a
+// (position, head) pair, row r -> position r / PACK, head r % PACK, fa2/kernel.py:135-141)
+// of one (batch, q-head block) and walks the K/V tiles [0, J) it can see, in increasing
+// order (the reference's order: stage 1 unmasked tiles from column 0, then the diagonal
+// band, nothing to its right; fa2/kernel.py:150-175).
+//
+// Warp roles (384 threads, three warpgroups):
+//   warps 0-3   softmax for Q tile 0   (thread = one row = one TMEM lane)
+//   warps 4-7   softmax for Q tile 1
+//   warp  8     tcgen05 MMA issue (one thread) + TMEM allocation
+//   warp  9     TMA producer (one thread)
+//   warps 10-11 idle
+// Registers: launched at 168/thread; setmaxnreg moves them to the softmax warpgroups
+// (208 each) from the MMA/TMA warpgroup (88): 2 * 208 + 88 == 3 * 168.
+// TMEM (512 columns x 128 lanes, fp32):  S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [..+D)
+//   P_t (fp16/bf16, packed 2 per column) overwrites the upper half of S_t, and the second
+//   GEMM reads it straight from TMEM (tcgen05.mma A-from-TMEM).
+// MMA order per K/V step j:  PV(0,j) QK(0,j+1) PV(1,j) QK(1,j+1)  -- while softmax 0 works
+//   on S0 the tensor core runs tile 1's GEMMs and vice versa (ping-pong).
+//
+// Online softmax (fa2/kernel.py:90-106) in base 2 with one FFMA per score,
+// p = exp2(s * qk_scale - m); l and O accumulate in fp32; P is rounded to the input dtype
+// before the PV GEMM (fa2/kernel.py:104-105). The running max is only moved when a row's
+// max grows by more than 2^8 (the O and l rescale is then skipped exactly, alpha == 1); the
+// final O / l is unchanged because O and l always share the same reference max.
+//
+// Every mbarrier wait is bounded (mbar_wait); a role that gives up raises FA2_ERR_TIMEOUT
+// in the caller's error word and joins the common teardown, so no wait can hang the GPU.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+
+#include "exp2_poly.cuh"
+#include "fa2_sm100.h"
+#include "ptx_sm100.cuh"
+
+namespace fa2 {
+
+constexpr int BM = 128;  // rows per Q tile (one TMEM lane each)
+constexpr int BN = 128;  // K/V rows per tile
+constexpr int Q_TILES = 2;
+constexpr int NUM_WARPS = 12;
+constexpr int NUM_THREADS = NUM_WARPS * 32;
+constexpr int MMA_WARP = 8;
+constexpr int LOAD_WARP = 9;
+constexpr int TMEM_COLS = 512;
+constexpr int REGS_SOFTMAX = 208;
+constexpr int REGS_OTHER = 88;
+constexpr float RESCALE_TH = 8.0f;               // log2 units: P may reach 2^8 before a rescale
+constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
+constexpr uint32_t EMU_PAIR_MASK = 0x2222u;      // pairs 1,5,9,13 of every 16: 25% of exp2 on FMA
+
+template <int D>
+struct Cfg {
+  static_assert(D == 64 || D == 128, "compiled head dims");
+  static constexpr int CHUNKS = D / 64;             // 64-element (128-byte) swizzle atoms along d
+  static constexpr int CHUNK_BYTES = 128 * 128;     // 128 rows x 128 bytes
+  static constexpr int TILE_BYTES = BN * D * 2;     // == BM * D * 2
+  static constexpr int STAGES = (D == 128) ? 4 : 8; // K/V ring depth (K_j and V_j take one slot each)
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = Q_TILES * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + STAGES * TILE_BYTES;
+  // barrier slots
+  static constexpr int B_Q = 0;                     // [2]  Q tile landed
+  static constexpr int B_KV_FULL = 2;               // [S]  K/V tile landed
+  static constexpr int B_KV_EMPTY = 2 + STAGES;     // [S]  K/V slot released by the MMAs
+  static constexpr int B_S_FULL = 2 + 2 * STAGES;   // [2]  S_t in TMEM
+  static constexpr int B_P_FULL = 4 + 2 * STAGES;   // [2]  P_t in TMEM (and O_t rescaled)
+  static constexpr int B_O_FULL = 6 + 2 * STAGES;   // [2]  last PV of tile t retired
+  static constexpr int B_MMA_DONE = 8 + 2 * STAGES; // [1]  every MMA retired (teardown)
+  static constexpr int NUM_BARS = 9 + 2 * STAGES;
+  static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
+  static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
+  static constexpr int TMEM_O = 2 * BN;                 // O_t at TMEM_O + t * D
+  static_assert(TMEM_O + 2 * D <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
+};
+
+struct KArgs {
+  int n_q, n_kv, group, pack, hblocks;  // hblocks = H_q / pack
+  float qk_scale;
+  int* err;
+  long long timeout;
+};
+
+// ---------------------------------------------------------------- softmax helpers
+
+// Row max of 128 scores with four independent 3-input max chains.
+__device__ __forceinline__ float row_max128(const uint32_t (&s)[4][32]) {
+  float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      m0 = fmax3(m0, __uint_as_float(s[c][i + 0]), __uint_as_float(s[c][i + 1]));
+      m1 = fmax3(m1, __uint_as_float(s[c][i + 2]), __uint_as_float(s[c][i + 3]));
+      m2 = fmax3(m2, __uint_as_float(s[c][i + 4]), __uint_as_float(s[c][i + 5]));
+      m3 = fmax3(m3, __uint_as_float(s[c][i + 6]), __uint_as_float(s[c][i + 7]));
+    }
+  }
+  return fmax3(fmaxf(m0, m1), m2, m3);
+}
+
+// p = exp2(s * scale - m) for 32 scores, packed to 16 words of (lo, hi) halves, and
+// accumulated into two packed fp32 partial sums. EMU: a fixed subset of pairs is computed
+// on the FMA pipe (exp2_poly_x2); the subset depends only on the column index.
+template <bool BF16, bool EMU>
+__device__ __forceinline__ void make_p32(const uint32_t (&s)[32], uint64_t sc2, uint64_t nm2,
+                                         uint32_t (&pk)[16], uint64_t& sum_a, uint64_t& sum_b) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), sc2, nm2);
+    float x0, x1, p0, p1;
+    f2_unpack(x2, x0, x1);
+    if (EMU && ((EMU_PAIR_MASK >> e) & 1u)) {
+      exp2_poly_x2<BF16 ? 3 : 4>(x0, x1, p0, p1);
+    } else {
+      p0 = ex2_mufu(x0);
+      p1 = ex2_mufu(x1);
+    }
+    pk[e] = cvt_pack2<BF16>(p0, p1);
+    if (e & 1) {
+      sum_b = f2_add(sum_b, f2_pack(p0, p1));
+    } else {
+      sum_a = f2_add(sum_a, f2_pack(p0, p1));
+    }
+  }
+}
+
+// O_t row *= alpha (this thread's TMEM lane), 32 columns at a time.
+template <int D>
+__device__ __forceinline__ void rescale_o_row(uint32_t tO, float alpha) {
+  const uint64_t a2 = f2_pack(alpha, alpha);
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t o[32];
+    tmem_ld32(tO + c * 32, o);
+    tmem_wait_ld();
+    reg_fence32(o);
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float a, b;
+      f2_unpack(f2_mul(f2_pack(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), a2), a, b);
+      o[i] = __float_as_uint(a);
+      o[i + 1] = __float_as_uint(b);
+    }
+    tmem_st32(tO + c * 32, o);
+  }
+  tmem_wait_st();
+}
+
+// ------------------------------------------------------------------------ kernel
+template <int D, bool CAUSAL, bool BF16>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+               const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+               const KArgs a) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t sraw = smem_u32(smem_raw);
+  const uint32_t sbase = (sraw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (sbase - sraw);
+  auto bar = [&](int i) -> uint32_t { return sbase + C::OFF_BAR + 8u * static_cast<uint32_t>(i); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Work unit: (batch b, q-head block hb) on x, 256-row block on y (heaviest causal first).
+  const int b = blockIdx.x / a.hblocks;
+  const int hq0 = (blockIdx.x % a.hblocks) * a.pack;
+  const int hkv = hq0 / a.group;
+  const int mb = CAUSAL ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : static_cast<int>(blockIdx.y);
+  const int row0 = mb * (Q_TILES * BM);  // first packed row of this CTA
+  int kv_end = a.n_kv;
+  if (CAUSAL) {
+    const int last_pos = min((row0 + Q_TILES * BM - 1) / a.pack, a.n_q - 1);
+    kv_end = min(last_pos + 1, a.n_kv);
+  }
+  const int J = (kv_end + BN - 1) / BN;  // K/V tiles visited by this CTA (>= 1)
+
+  if (warp == LOAD_WARP && lane == 0) {
+    mbar_init(bar(C::B_Q + 0), 1);
+    mbar_init(bar(C::B_Q + 1), 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar(C::B_KV_FULL + s), 1);
+      mbar_init(bar(C::B_KV_EMPTY + s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(C::B_S_FULL + t), 1);
+      mbar_init(bar(C::B_P_FULL + t), BM);
+      mbar_init(bar(C::B_O_FULL + t), 1);
+    }
+    mbar_init(bar(C::B_MMA_DONE), 1);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == MMA_WARP) {
+    __syncwarp();
+    tmem_alloc(sbase + C::OFF_TMEM_PTR, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_TMEM_PTR);
+
+  bool ok = true;
+
+  if (warp == LOAD_WARP) {
+    reg_dealloc<REGS_OTHER>();
+    // ------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      tma_prefetch_desc(&tmO);
+      const uint64_t pol_kv = l2_policy_evict_last();   // K/V are re-read by every Q block
+      const uint64_t pol_q = l2_policy_evict_first();   // Q is read once
+      auto load_q = [&](int t) {
+        const int R = row0 + t * BM;
+        const int pos = R / a.pack;
+        const int h = hq0 + R % a.pack;
+        mbar_arrive_expect_tx(bar(C::B_Q + t), C::TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c) {
+          tma_load_4d(sbase + C::OFF_Q + t * C::TILE_BYTES + c * C::CHUNK_BYTES, &tmQ, bar(C::B_Q + t),
+                      c * 64, h, pos, b, pol_q);
+        }
+      };
+      load_q(0);
+      int issued = 0;
+      for (int i = 0; i < 2 * J; ++i) {
+        const int st = i % C::STAGES;
+        const uint32_t ph = static_cast<uint32_t>(i / C::STAGES) & 1u;
+        if (!mbar_wait(bar(C::B_KV_EMPTY + st), ph ^ 1u, a.timeout, a.err)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(bar(C::B_KV_FULL + st), C::TILE_BYTES);
+        const CUtensorMap* m = (i & 1) ? &tmV : &tmK;
+#pragma unroll
+        for (int c = 0; c < C::CHUNKS; ++c) {
+          tma_load_4d(sbase + C::OFF_KV + st * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
+                      bar(C::B_KV_FULL + st), c * 64, (i >> 1) * BN, hkv, b, pol_kv);
+        }
+        ++issued;
+        if (i == 0) load_q(1);
+      }
+      // Drain: every TMA write into this CTA's shared memory must land before the CTA
+      // can exit, also when another role gave up early.
+      for (int i = max(0, issued - C::STAGES); i < issued; ++i) {
+        mbar_wait(bar(C::B_KV_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
+                  a.timeout, nullptr);
+      }
+      mbar_wait(bar(C::B_Q + 0), 0, a.timeout, nullptr);
+      if (issued > 0) mbar_wait(bar(C::B_Q + 1), 0, a.timeout, nullptr);
+    }
+  } else if (warp == MMA_WARP) {
+    reg_dealloc<REGS_OTHER>();
+    // -------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
+      constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, true);
+      auto issue_qk = [&](int t, int st) {
+        const uint32_t qa = sbase + C::OFF_Q + t * C::TILE_BYTES;
+        const uint32_t ka = sbase + C::OFF_KV + st * C::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::CHUNK_BYTES + (kk & 3) * 32;
+          mma_ss(tmem + t * BN, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024),
+                 idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int t, int st, bool acc) {
+        const uint32_t va = sbase + C::OFF_KV + st * C::TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          mma_ts(tmem + C::TMEM_O + t * D, tmem + t * BN + BN / 2 + kk * 8,
+                 sdesc_sw128(va + kk * 16 * 128, C::CHUNK_BYTES, 1024), idesc_pv,
+                 (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+      auto kv_wait = [&](int i) -> bool {
+        return mbar_wait(bar(C::B_KV_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
+                         a.timeout, a.err);
+      };
+      do {
+        if (!mbar_wait(bar(C::B_Q + 0), 0, a.timeout, a.err) || !kv_wait(0)) { ok = false; break; }
+        tc_fence_after();
+        issue_qk(0, 0);
+        mma_commit(bar(C::B_S_FULL + 0));
+        if (!mbar_wait(bar(C::B_Q + 1), 0, a.timeout, a.err)) { ok = false; break; }
+        tc_fence_after();
+        issue_qk(1, 0);
+        mma_commit(bar(C::B_S_FULL + 1));
+        mma_commit(bar(C::B_KV_EMPTY + 0));
+        for (int j = 0; j < J; ++j) {
+          const int iv = 2 * j + 1, ik = 2 * j + 2;
+          const int sv = iv % C::STAGES, sk = ik % C::STAGES;
+          const bool more = (j + 1 < J);
+          const uint32_t pph = static_cast<uint32_t>(j) & 1u;
+          if (!kv_wait(iv) || !mbar_wait(bar(C::B_P_FULL + 0), pph, a.timeout, a.err)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(0, sv, j > 0);
+          if (more) {
+            if (!kv_wait(ik)) { ok = false; break; }
+            tc_fence_after();
+            issue_qk(0, sk);
+            mma_commit(bar(C::B_S_FULL + 0));
+          } else {
+            mma_commit(bar(C::B_O_FULL + 0));
+          }
+          if (!mbar_wait(bar(C::B_P_FULL + 1), pph, a.timeout, a.err)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(1, sv, j > 0);
+          mma_commit(bar(C::B_KV_EMPTY + sv));
+          if (more) {
+            issue_qk(1, sk);
+            mma_commit(bar(C::B_S_FULL + 1));
+            mma_commit(bar(C::B_KV_EMPTY + sk));
+          } else {
+            mma_commit(bar(C::B_O_FULL + 1));
+          }
+        }
+      } while (false);
+      // Every issued MMA must retire before TMEM is released.
+      mma_commit(bar(C::B_MMA_DONE));
+      mbar_wait(bar(C::B_MMA_DONE), 0, a.timeout, nullptr);
+    }
+  } else if (warp < 8) {
+    reg_alloc<REGS_SOFTMAX>();
+    // ------------------------------------------------------------------ softmax
+    const int t = warp >> 2;          // Q tile
+    const int q = warp & 3;           // TMEM lane quadrant of this warp
+    const int r = q * 32 + lane;      // row within the tile == TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + t * BN;
+    const uint32_t tP = tS + BN / 2;
+    const uint32_t tO = tmem + lane_addr + C::TMEM_O + t * D;
+    const int tile_row0 = row0 + t * BM;
+    const int pos = (tile_row0 + r) / a.pack;    // sequence position of this row
+    const int tile_pos0 = tile_row0 / a.pack;    // position of the tile's first row
+    const float qk_scale = a.qk_scale;
+    const uint64_t sc2 = f2_pack(qk_scale, qk_scale);
+
+    float m_use = -INFINITY;  // reference max of this row (scaled, base 2)
+    float l = 0.0f;
+    for (int j = 0; j < J; ++j) {
+      bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(j) & 1u, a.timeout, a.err);
+      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
+
+      const int col0 = j * BN;
+      const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
+      const bool need_pad = (col0 + BN > a.n_kv);
+      const bool masked = need_causal || need_pad;  // uniform over the warpgroup
+      if (masked) {
+        int lim = a.n_kv - 1 - col0;  // last visible column of this tile, relative
+        if (CAUSAL) lim = min(lim, pos - col0);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (c * 32 + i > lim) s[c][i] = __float_as_uint(-INFINITY);
+          }
+        }
+      }
+      const float m_cand = row_max128(s) * qk_scale;
+      const bool bump = m_cand > m_use + RESCALE_TH;  // first tile: always (m_use = -inf)
+      float alpha = 1.0f;
+      if (bump) {
+        alpha = ex2_mufu(m_use - m_cand);
+        m_use = m_cand;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, bump)) {
+        // PV(t, j-1) has retired: S_t(j) was committed after it.
+        rescale_o_row<D>(tO, alpha);
+      }
+      l *= alpha;
+
+      const uint64_t nm2 = f2_pack(-m_use, -m_use);
+      uint64_t sum_a = f2_pack(0.0f, 0.0f), sum_b = f2_pack(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+        if (masked) {
+          make_p32<BF16, false>(s[c], sc2, nm2, pk, sum_a, sum_b);
+        } else {
+          make_p32<BF16, true>(s[c], sc2, nm2, pk, sum_a, sum_b);
+        }
+        tmem_st16(tP + c * 16, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(C::B_P_FULL + t));
+      float sa0, sa1, sb0, sb1;
+      f2_unpack(sum_a, sa0, sa1);
+      f2_unpack(sum_b, sb0, sb1);
+      l += (sa0 + sa1) + (sb0 + sb1);
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    if (ok) {
+      bool w = mbar_wait(bar(C::B_O_FULL + t), 0, a.timeout, a.err);
+      if (!__all_sync(0xffffffffu, w)) ok = false;
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.0f / l;
+      const uint32_t so = sbase + C::OFF_Q + t * C::TILE_BYTES;  // Q_t is dead: reuse as staging
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          pk[e] = cvt_pack2<BF16>(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
+        }
+        const uint32_t row_addr = so + (c >> 1) * C::CHUNK_BYTES + r * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t unit = static_cast<uint32_t>((c & 1) * 4 + u);
+          st_shared_v4(row_addr + ((unit ^ static_cast<uint32_t>(r & 7)) << 4), pk[4 * u], pk[4 * u + 1],
+                       pk[4 * u + 2], pk[4 * u + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int R0 = tile_row0 + q * 32;
+        const int pos0 = R0 / a.pack;
+        const int h0 = hq0 + R0 % a.pack;
+        if (pos0 < a.n_q) {
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; ++c) {
+            tma_store_4d(&tmO, so + c * C::CHUNK_BYTES + q * 32 * 128, c * 64, h0, pos0, b);
+          }
+          bulk_commit();
+          bulk_wait_all();
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    reg_dealloc<REGS_OTHER>();  // warps 10-11: nothing to do
+  }
+
+  if (!ok && a.err != nullptr) atomicOr(a.err, FA2_ERR_TIMEOUT);
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace fa2
+
+// =============================================================================== host
+
+namespace {
+
+using fa2::Cfg;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = []() -> PFN_cuTensorMapEncodeTiled_v12000 {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult qr{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &qr) !=
+            cudaSuccess ||
+        qr != cudaDriverEntryPointSuccess) {
+      return nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 4-D tiled map, 128-byte swizzle, zero fill out of bounds. dims/strides in elements.
+bool make_map(CUtensorMap* m, bool bf16, const void* base, const int64_t dims[4], const int64_t strides[4],
+              const uint32_t box[4]) {
+  cuuint64_t gdim[4];
+  cuuint64_t gstride[3];
+  cuuint32_t bdim[4];
+  cuuint32_t estride[4] = {1, 1, 1, 1};
+  for (int i = 0; i < 4; ++i) {
+    gdim[i] = static_cast<cuuint64_t>(dims[i]);
+    bdim[i] = box[i];
+  }
+  for (int i = 1; i < 4; ++i) {
+    // The stride of an extent-1 dimension is never used; give TMA a legal value.
+    const int64_t s = dims[i] > 1 ? strides[i] : 8;
+    gstride[i - 1] = static_cast<cuuint64_t>(s) * 2u;
+  }
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                        const_cast<void*>(base), gdim, gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+constexpr int kMaxDevices = 64;
+
+template <int D, bool CAUSAL, bool BF16>
+int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
+  using C = Cfg<D>;
+  auto kern = fa2::fa2_fwd_kernel<D, CAUSAL, BF16>;
+  static bool attr_done[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) return FA2_ERR_DEVICE;
+  if (!attr_done[device]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC) != cudaSuccess) {
+      return FA2_ERR_LAUNCH;
+    }
+    attr_done[device] = true;
+  }
+  const int group = p->heads_q / p->heads_kv;
+  const int pack = p->pack_gqa ? group : 1;
+
+  // Q / O: dims (d, h, n, b). A box row is a (position, head) pair, heads fastest, so a
+  // packed tile is exactly rows r -> (position r / PACK, head r % PACK).
+  CUtensorMap tmQ, tmK, tmV, tmO;
+  const int64_t qdims[4] = {D, p->heads_q, p->seqlen_q, p->batch};
+  const int64_t qstr[4] = {1, p->q_stride[1], p->q_stride[2], p->q_stride[0]};
+  const int64_t ostr[4] = {1, p->o_stride[1], p->o_stride[2], p->o_stride[0]};
+  const uint32_t gh_q = static_cast<uint32_t>(pack);           // heads per 128-row Q box
+  const uint32_t qbox[4] = {64, gh_q, 128u / gh_q, 1};
+  const uint32_t gh_o = static_cast<uint32_t>(pack < 32 ? pack : 32);  // 32-row O box per warp
+  const uint32_t obox[4] = {64, gh_o, 32u / gh_o, 1};
+  // K / V: dims (d, n, h, b), 128-row boxes of one head.
+  const int64_t kdims[4] = {D, p->seqlen_kv, p->heads_kv, p->batch};
+  const int64_t kstr[4] = {1, p->k_stride[2], p->k_stride[1], p->k_stride[0]};
+  const int64_t vstr[4] = {1, p->v_stride[2], p->v_stride[1], p->v_stride[0]};
+  const uint32_t kvbox[4] = {64, static_cast<uint32_t>(fa2::BN), 1, 1};
+  const bool bf16 = (p->dtype == FA2_DTYPE_BF16);
+  if (!make_map(&tmQ, bf16, p->q, qdims, qstr, qbox) || !make_map(&tmO, bf16, p->o, qdims, ostr, obox) ||
+      !make_map(&tmK, bf16, p->k, kdims, kstr, kvbox) || !make_map(&tmV, bf16, p->v, kdims, vstr, kvbox)) {
+    return FA2_ERR_TMA_ENCODE;
+  }
+
+  fa2::KArgs ka;
+  ka.n_q = p->seqlen_q;
+  ka.n_kv = p->seqlen_kv;
+  ka.group = group;
+  ka.pack = pack;
+  ka.hblocks = p->heads_q / pack;
+  ka.qk_scale = p->qk_scale;
+  ka.err = p->err_flag;
+  ka.timeout = p->timeout_cycles > 0 ? p->timeout_cycles : fa2::DEFAULT_TIMEOUT;
+
+  const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
+  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(p->batch) * ka.hblocks),
+                  static_cast<unsigned>((rows + fa2::Q_TILES * fa2::BM - 1) / (fa2::Q_TILES * fa2::BM)));
+  kern<<<grid, fa2::NUM_THREADS, C::SMEM_ALLOC, stream>>>(tmQ, tmK, tmV, tmO, ka);
+  if (cudaGetLastError() != cudaSuccess) return FA2_ERR_LAUNCH;
+  return FA2_OK;
+}
+
+template <int D>
+int dispatch_d(const Fa2FwdParams* p, cudaStream_t s, int dev) {
+  const bool bf16 = p->dtype == FA2_DTYPE_BF16;
+  if (p->causal) return bf16 ? launch<D, true, true>(p, s, dev) : launch<D, true, false>(p, s, dev);
+  return bf16 ? launch<D, false, true>(p, s, dev) : launch<D, false, false>(p, s, dev);
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Strides of a [B, H, N, D] operand: d stride 1, others multiples of 8 elements (16 B),
+// non-negative. Extent-1 dimensions are exempt (their stride is never used).
+bool layout_ok(const int64_t st[4], const int64_t ext[4]) {
+  if (ext[3] > 1 && st[3] != 1) return false;
+  for (int i = 0; i < 3; ++i) {
+    if (ext[i] <= 1) continue;
+    if (st[i] < 0 || (st[i] % 8) != 0 || st[i] >= (int64_t(1) << 38)) return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa2_sm100_abi_version(void) { return FA2_SM100_ABI_VERSION; }
+
+int64_t fa2_sm100_params_size(void) { return static_cast<int64_t>(sizeof(Fa2FwdParams)); }
+
+const char* fa2_sm100_strerror(int status) {
+  switch (status) {
+    case FA2_OK: return "ok";
+    case FA2_ERR_NULL: return "a required pointer is NULL";
+    case FA2_ERR_SHAPE: return "invalid shape (sizes, batch/head_dim mismatch, or causal with N_q != N_kv)";
+    case FA2_ERR_DTYPE: return "dtype must be fp16 or bf16";
+    case FA2_ERR_HEAD_DIM: return "head_dim not supported by the compiled sm_100a kernels (64, 128)";
+    case FA2_ERR_GQA: return "H_q must be divisible by H_kv";
+    case FA2_ERR_PACK: return "pack_gqa needs the GQA group to divide BLOCK_M (128)";
+    case FA2_ERR_SCALE: return "qk_scale must be finite and > 0";
+    case FA2_ERR_LAYOUT: return "strides/alignment not usable by TMA (d stride 1, others multiples of 16 bytes, 16-byte aligned bases)";
+    case FA2_ERR_TMA_ENCODE: return "cuTensorMapEncodeTiled rejected a tensor map";
+    case FA2_ERR_LAUNCH: return "kernel launch failed";
+    case FA2_ERR_DEVICE: return "current device is not sm_100 (B200) or the CUDA driver entry point is missing";
+    case FA2_ERR_TIMEOUT: return "a bounded wait inside the kernel expired";
+    default: return "unknown fa2_sm100 status";
+  }
+}
+
+int fa2_fwd_sm100_config(int32_t head_dim, int32_t* block_m, int32_t* block_n, int32_t* threads,
+                         int32_t* stages, int32_t* smem_bytes) {
+  int st = 0, sm = 0;
+  if (head_dim == 64) {
+    st = Cfg<64>::STAGES;
+    sm = Cfg<64>::SMEM_ALLOC;
+  } else if (head_dim == 128) {
+    st = Cfg<128>::STAGES;
+    sm = Cfg<128>::SMEM_ALLOC;
+  } else {
+    return FA2_ERR_HEAD_DIM;
+  }
+  if (block_m) *block_m = fa2::BM;
+  if (block_n) *block_n = fa2::BN;
+  if (threads) *threads = fa2::NUM_THREADS;
+  if (stages) *stages = st;
+  if (smem_bytes) *smem_bytes = sm;
+  return FA2_OK;
+}
+
+int fa2_fwd_sm100_check(const Fa2FwdParams* p) {
+  if (p == nullptr || p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr) return FA2_ERR_NULL;
+  if (p->batch < 1 || p->heads_q < 1 || p->heads_kv < 1 || p->seqlen_q < 0 || p->seqlen_kv < 1) return FA2_ERR_SHAPE;
+  if (p->causal && p->seqlen_q != p->seqlen_kv) return FA2_ERR_SHAPE;
+  if (p->dtype != FA2_DTYPE_FP16 && p->dtype != FA2_DTYPE_BF16) return FA2_ERR_DTYPE;
+  if (p->head_dim != 64 && p->head_dim != 128) return FA2_ERR_HEAD_DIM;
+  if (p->heads_q % p->heads_kv != 0) return FA2_ERR_GQA;
+  const int group = p->heads_q / p->heads_kv;
+  if (p->pack_gqa && (fa2::BM % group) != 0) return FA2_ERR_PACK;
+  if (!(std::isfinite(p->qk_scale) && p->qk_scale > 0.0f)) return FA2_ERR_SCALE;
+  const int pack = p->pack_gqa ? group : 1;
+  const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
+  if ((rows + 255) / 256 > 65535) return FA2_ERR_SHAPE;
+  if (static_cast<int64_t>(p->batch) * (p->heads_q / pack) > 0x7fffffffLL) return FA2_ERR_SHAPE;
+  const int64_t qext[4] = {p->batch, p->heads_q, p->seqlen_q, p->head_dim};
+  const int64_t kext[4] = {p->batch, p->heads_kv, p->seqlen_kv, p->head_dim};
+  if (!layout_ok(p->q_stride, qext) || !layout_ok(p->o_stride, qext) || !layout_ok(p->k_stride, kext) ||
+      !layout_ok(p->v_stride, kext)) {
+    return FA2_ERR_LAYOUT;
+  }
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o)) return FA2_ERR_LAYOUT;
+  return FA2_OK;
+}
+
+int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream) {
+  const int rc = fa2_fwd_sm100_check(p);
+  if (rc != FA2_OK) return rc;
+  if (p->seqlen_q == 0) return FA2_OK;
+  int dev = -1, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FA2_ERR_DEVICE;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+    return FA2_ERR_DEVICE;
+  }
+  if (major != 10 || minor != 0) return FA2_ERR_DEVICE;
+  if (encode_fn() == nullptr) return FA2_ERR_DEVICE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return p->head_dim == 64 ? dispatch_d<64>(p, s, dev) : dispatch_d<128>(p, s, dev);
+}
+
+}  // extern "C"

@@ -1,0 +1,173 @@
+"""FlashAttention-2 forward on Blackwell (sm_100a): the drop-in for the reference's
+`fa2.kernel` module (roy6n23/triton-fa2-forward, fa2/kernel.py).
+
+Same public surface as the reference:
+    attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
+              num_warps=None, num_stages=None, pack_gqa=None)        fa2/kernel.py:210-260
+    should_pack_gqa(n_q, group, block_m)                             fa2/kernel.py:202-207
+    _default_config(head_dim, on_cuda)                               fa2/kernel.py:186-195
+
+q: [B, H_q, N_q, D]; k, v: [B, H_kv, N_kv, D] (any strides); H_q % H_kv == 0; fp16/bf16;
+returns out = softmax(q k^T * sm_scale [+ top-left causal mask]) v with q's strides.
+The computation is the hand-written sm_100a CUDA kernel in csrc/fa2_fwd_sm100.cu, reached
+through the C ABI of include/fa2_sm100.h. There is no Triton and no CPU path: tensors not
+on an sm_100 CUDA device raise RuntimeError.
+
+Differences from the reference that do not change results:
+  * The compiled tile is 128 x 128 (two 128-row Q tiles per CTA). block_m / block_n /
+    num_warps / num_stages are accepted as hints: block_m feeds the GQA-packing decision and
+    its ValueError exactly as in the reference; the others do not change the kernel.
+  * Packed and unpacked runs are bit-identical (same tiles, same order, per-row decisions),
+    so a group that divides the hinted block_m but not 128 simply runs unpacked.
+  * head_dim 16 and 32 run the 64 kernel on zero-padded copies (extra zero columns add
+    nothing to QK^T and produce zero output columns that are dropped).
+"""
+
+import math
+
+import torch
+
+from . import _lib
+
+LOG2E = 1.4426950408889634
+KERNEL_BLOCK_M = 128
+KERNEL_BLOCK_N = 128
+
+_err_words = {}
+
+
+def _default_config(head_dim, on_cuda):
+    """(BLOCK_M, BLOCK_N, num_warps, num_stages) of the compiled sm_100a kernel for head_dim.
+
+    Mirrors fa2/kernel.py:186-195. `on_cuda` is accepted for signature compatibility; there
+    is only one (CUDA) implementation, so it does not change the answer.
+    """
+    del on_cuda
+    d = 64 if head_dim <= 64 else 128
+    bm, bn, threads, stages, _ = _lib.config(d)
+    return bm, bn, threads // 32, stages
+
+
+def _tile_efficiency(rows, block_m):
+    return rows / (-(-rows // block_m) * block_m)
+
+
+def should_pack_gqa(n_q, group, block_m):
+    """FlashAttention-3's rule, as in fa2/kernel.py:202-207: pack when the unpacked tiles are
+    less than 90% as full as the packed ones; packing needs block_m % group == 0."""
+    if group == 1 or block_m % group:
+        return False
+    return _tile_efficiency(n_q, block_m) < 0.9 * _tile_efficiency(n_q * group, block_m)
+
+
+def _err_word(device):
+    """Per-device int32 that the kernel ORs FA2_ERR_TIMEOUT into when a bounded wait expires."""
+    key = device.index
+    w = _err_words.get(key)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=device)
+        _err_words[key] = w
+    return w
+
+
+def check_device_errors(device=None):
+    """Synchronise `device` and raise RuntimeError if a kernel reported a timed-out wait
+    since the last check (the word is cleared). Launches never synchronise on their own."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    w = _err_words.get(device.index)
+    if w is None:
+        return
+    val = int(w.item())
+    if val:
+        w.zero_()
+        raise RuntimeError(f"fa2 sm100 kernel reported status {val}: {_lib.strerror(val)}")
+
+
+def _strides(t):
+    return tuple(int(s) for s in t.stride())
+
+
+def _launch(q, k, v, out, causal, pack, qk_scale, timeout_cycles=0):
+    B, H_q, N_q, D = q.shape
+    H_kv, N_kv = k.shape[1], k.shape[2]
+    err = _err_word(q.device)
+    p = _lib.make_params(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+        _strides(q), _strides(k), _strides(v), _strides(out),
+        B, H_q, H_kv, N_q, N_kv, D,
+        _lib.FA2_DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.FA2_DTYPE_FP16,
+        causal, pack, qk_scale, err.data_ptr(), timeout_cycles,
+    )
+    stream = torch.cuda.current_stream(q.device).cuda_stream
+    return _lib.launch(p, stream)
+
+
+def _run(q, k, v, out, causal, pack, qk_scale):
+    with torch.cuda.device(q.device):
+        rc = _launch(q, k, v, out, causal, pack, qk_scale)
+        if rc == _lib.FA2_ERR_TMA_ENCODE and pack:
+            pack = False  # bit-identical result; some stride orders only encode unpacked
+            rc = _launch(q, k, v, out, causal, pack, qk_scale)
+        if rc in (_lib.FA2_ERR_LAYOUT, _lib.FA2_ERR_TMA_ENCODE):
+            # Layout copy (not a compute fallback): TMA needs 16-byte strides/alignment.
+            qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+            oc = torch.empty_like(qc)
+            rc = _launch(qc, kc, vc, oc, causal, pack, qk_scale)
+            if rc == _lib.FA2_OK:
+                out.copy_(oc)
+        if rc != _lib.FA2_OK:
+            raise _lib.Fa2Error(rc, _lib.strerror(rc))
+    return out
+
+
+def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
+              num_warps=None, num_stages=None, pack_gqa=None):
+    """softmax(Q K^T * sm_scale [+ causal mask]) V, fused (fa2/kernel.py:210-260).
+
+    q: [B, H_q, N_q, D]; k, v: [B, H_kv, N_kv, D]; returns [B, H_q, N_q, D].
+    pack_gqa: put each GQA group's query heads into one tile; None decides with
+    should_pack_gqa. Asynchronous on torch's current stream, like the reference.
+    """
+    assert q.dim() == k.dim() == v.dim() == 4
+    B, H_q, N_q, D = q.shape
+    Bk, H_kv, N_kv, Dk = k.shape
+    assert v.shape == k.shape and Bk == B and Dk == D
+    assert q.dtype == k.dtype == v.dtype and q.dtype in (torch.float16, torch.bfloat16)
+    assert H_q % H_kv == 0, "GQA needs H_q divisible by H_kv"
+    assert D in (16, 32, 64, 128), "head_dim must be a power of two in [16, 128]"
+    if causal:
+        # Top-left aligned causal mask (prefill), as in the reference.
+        assert N_q == N_kv, "causal attention here assumes N_q == N_kv"
+
+    bm, bn, nw, ns = _default_config(D, q.is_cuda)
+    bm, bn = block_m or bm, block_n or bn
+    nw, ns = num_warps or nw, num_stages or ns
+    group = H_q // H_kv
+    if pack_gqa is None:
+        pack_gqa = should_pack_gqa(N_q, group, bm)
+    elif pack_gqa and bm % group:
+        raise ValueError(f"pack_gqa needs BLOCK_M ({bm}) to be a multiple of the GQA group ({group})")
+    pack = bool(pack_gqa) and group > 1 and KERNEL_BLOCK_M % group == 0
+
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if not sm_scale > 0:
+        raise ValueError(f"sm_scale must be positive (the row max is scaled after it is taken), got {sm_scale}")
+    qk_scale = sm_scale * LOG2E
+
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("fa2.kernel.attention runs only on an sm_100 CUDA device (no CPU path)")
+    if not (q.device == k.device == v.device):
+        raise RuntimeError("q, k and v must be on the same CUDA device")
+
+    out = torch.empty_like(q)
+    if out.numel() == 0:
+        return out
+    if D < 64:
+        pad = (0, 64 - D)
+        qp, kp, vp = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
+        op = torch.empty_like(qp)
+        _run(qp, kp, vp, op, causal, pack, qk_scale)
+        out.copy_(op[..., :D])
+        return out
+    return _run(q, k, v, out, causal, pack, qk_scale)
