@@ -1,0 +1,380 @@
+"""Benchmark of the sm_100a FA2 forward on the reference's headline metric.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N
+
+Metric: attention forward TFLOP/s, bf16, causal, N=8192, D=128, GQA 32/8
+(B=2): FLOPs = 4 * B * H_q * D * N(N+1)/2 (the reference's count, bench/bench.py:83-87).
+A step is one forward over the whole workload. At N GPUs the (batch, kv-head) units are
+sharded (2 GPUs: 8 units each ... 8 GPUs: 2 each), no collective on the data path; `value`
+is the whole-job FLOP/s = all ranks' FLOPs / max over ranks of the device time.
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the
+launching stream; a 256 MiB buffer is written between steps (L2 flush, as the reference's
+bench/bench.py:54-58; the inputs, 335 MB, are also larger than the 126 MB L2). Barrier +
+synchronize on both sides of the timed region; max over ranks.
+`e2e` is the same metric through the public API fa2.kernel.attention with the inputs in
+pinned host memory: each step copies q/k/v host->device, runs the forward and copies the
+output back, all inside the timed region.
+`--impl reference` times the reference's CPU path (the naive fp32 formula of
+fa2/reference.py:22-32, restated in oracle/) on the host cores, rank 0 only.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(REPO, "triton-fa2-forward_b200")
+sys.path.insert(0, PKG)
+
+import torch  # noqa: E402
+
+HEADLINE = dict(B=2, Hq=32, Hkv=8, N=8192, D=128, causal=True, dtype="bf16")
+METRIC = "attn fwd TFLOP/s (bf16 causal N=8K D=128 GQA32/8) at 1/2/4/8 GPU; % tensor peak"
+UNIT = "TFLOP/s"
+FALLBACK_PEAK_TFLOPS = 1590.0  # profiling recipe fallback if MEASURED_PEAKS.json is absent
+L2_FLUSH_BYTES = 256 << 20
+PROFILE_TRAFFIC = os.path.join(REPO, "profiles", "fa2_fwd_headline_ncu.txt")
+
+
+def flops(B, Hq, N, D, causal):
+    pairs = N * (N + 1) / 2 if causal else N * N
+    return 4.0 * B * Hq * pairs * D
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_inputs(c, lo, hi, seed=0):
+    """Seeded N(0,1) q/k/v of the headline shape generated on the CPU (identical on every
+    box), sliced to units [lo, hi) = the rank's shard, as [1, units*G, N, D] / [1, units, N, D]."""
+    B, Hq, Hkv, N, D = c["B"], c["Hq"], c["Hkv"], c["N"], c["D"]
+    G = Hq // Hkv
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B * Hq, N, D, generator=g)[lo * G:hi * G]
+    k = torch.randn(B * Hkv, N, D, generator=g)[lo:hi]
+    v = torch.randn(B * Hkv, N, D, generator=g)[lo:hi]
+    return tuple(t.to(torch.bfloat16).unsqueeze(0).contiguous() for t in (q, k, v))
+
+
+def measured_peak():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, "fallback (profiling recipe, 1.59 PFLOP/s)"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary, if present
+    (a line 'traffic_bytes_per_launch: <int>')."""
+    try:
+        with open(PROFILE_TRAFFIC) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(float(line.split(":", 1)[1].strip()))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [p.strip() for p in line.split(",")]
+                    if len(parts) >= 9:
+                        rows.append(parts)
+            os.unlink(self.path)
+        except OSError:
+            return None
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower().startswith("active")})
+        loaded = [x for x in sm if mx and x > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_baseline_sample(seconds=12.0, threads=None):
+    """Reference CPU path (naive fp32, oracle restatement of fa2/reference.py:22-32) on one
+    (batch, kv-head) unit of the headline config at a time, for about `seconds`."""
+    sys.path.insert(0, REPO)
+    from oracle.reference import naive_attention
+
+    if threads:
+        torch.set_num_threads(threads)
+    c = HEADLINE
+    G = c["Hq"] // c["Hkv"]
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, G, c["N"], c["D"], generator=g)
+    k = torch.randn(1, 1, c["N"], c["D"], generator=g)
+    v = torch.randn(1, 1, c["N"], c["D"], generator=g)
+    naive_attention(q[:, :, :512], k[:, :, :512], v[:, :, :512], causal=True)  # warm the BLAS
+    units, t0 = 0, time.perf_counter()
+    while True:
+        naive_attention(q, k, v, causal=True)
+        units += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    fl = units * flops(1, G, c["N"], c["D"], True)
+    return {"value": fl / el / 1e12, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{units} (batch, kv-head) unit(s) of the headline config (1x{G} q-heads x "
+                      f"{c['N']} x {c['D']}, causal) through oracle naive_attention in fp32 on the host, "
+                      f"{el:.1f} s"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's CPU path timed on the host cores (rank 0 only)."""
+    if rank != 0:
+        return 0
+    sys.path.insert(0, REPO)
+    from oracle.reference import naive_attention
+
+    c = HEADLINE
+    G = c["Hq"] // c["Hkv"]
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(1, G, c["N"], c["D"], generator=g)
+    k = torch.randn(1, 1, c["N"], c["D"], generator=g)
+    v = torch.randn(1, 1, c["N"], c["D"], generator=g)
+    for _ in range(args.warmup):
+        naive_attention(q, k, v, causal=True)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        naive_attention(q, k, v, causal=True)
+    el = time.perf_counter() - t0
+    step_fl = flops(1, G, c["N"], c["D"], True)
+    val = step_fl * args.steps / el / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "headline unit: B=1 Hq=4 Hkv=1 N=8192 D=128 causal (1 of 16 units per step)",
+                   "batch": 1, "heads_q": G, "heads_kv": 1, "seq_len": c["N"], "head_dim": c["D"],
+                   "causal": True, "parallelism": "host threads"},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": "one (batch, kv-head) unit of the headline config per step, naive fp32 "
+                                   "formula (oracle restatement of fa2/reference.py:22-32)"},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, world, rank, local):
+    from fa2.kernel import attention, check_device_errors
+    from fa2.shard import gather_output, shard_bounds
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    c = HEADLINE
+    lo, hi = shard_bounds(c["B"], c["Hkv"], rank, world)
+    G = c["Hq"] // c["Hkv"]
+    qh, kh, vh = make_inputs(c, lo, hi)
+    q, k, v = (t.to(dev) for t in (qh, kh, vh))
+    units = hi - lo
+    rank_flops = flops(1, units * G, c["N"], c["D"], True)
+    job_flops = flops(c["B"], c["Hq"], c["N"], c["D"], True)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def barrier():
+        if pg is not None:
+            t = torch.zeros(1, device=dev)
+            pg.all_reduce(t)
+        torch.cuda.synchronize(dev)
+
+    def step():
+        return attention(q, k, v, causal=True)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    check_device_errors(dev)
+
+    # ---- device-timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        barrier()
+        for s, e in ev:
+            flush.fill_(1)
+            s.record()
+            step()
+            e.record()
+        barrier()
+    check_device_errors(dev)
+    ms = [s.elapsed_time(e) for s, e in ev]
+    ms_sum = sum(ms)
+    ms_step = ms_sum / args.steps
+    if pg is not None:
+        t = torch.tensor([ms_step], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms_step_max = float(t.item())
+    else:
+        ms_step_max = ms_step
+    value = job_flops / (ms_step_max * 1e-3) / 1e12
+
+    # ---- optional replicated output: one NCCL all-gather of O (reported separately)
+    allgather_ms = None
+    if pg is not None and args.replicate_out:
+        out_shard = step()
+        for _ in range(2):
+            gather_output(out_shard, c["B"], c["Hq"], c["Hkv"])
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        gather_output(out_shard, c["B"], c["Hq"], c["Hkv"])
+        e.record()
+        barrier()
+        t = torch.tensor([s.elapsed_time(e)], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        allgather_ms = float(t.item())
+
+    # ---- end-to-end through the public API with pinned host buffers
+    qp, kp, vp = (t.pin_memory() for t in (qh, kh, vh))
+    out_host = torch.empty(qh.shape, dtype=qh.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in (qp, kp, vp))
+    d2h = out_host.numel() * out_host.element_size()
+    e2e_steps = max(1, min(args.steps, 10))
+
+    def e2e_step():
+        qd = qp.to(dev, non_blocking=True)
+        kd = kp.to(dev, non_blocking=True)
+        vd = vp.to(dev, non_blocking=True)
+        o = attention(qd, kd, vd, causal=True)
+        out_host.copy_(o, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e.record()
+    barrier()
+    e2e_ms = s.elapsed_time(e) / e2e_steps
+    if pg is not None:
+        t = torch.tensor([e2e_ms], device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    check_device_errors(dev)
+    e2e_value = job_flops / (e2e_ms * 1e-3) / 1e12
+
+    clocks = clk.summary()
+    peak, peak_src = measured_peak()
+    per_gpu_achieved = rank_flops / (ms_step * 1e-3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(seconds=args.cpu_seconds)
+
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step_max, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1), generated on CPU)",
+        "config": {"workload": "headline: B=2 Hq=32 Hkv=8 N=8192 D=128 bf16 causal",
+                   "batch": c["B"], "heads_q": c["Hq"], "heads_kv": c["Hkv"], "seq_len": c["N"],
+                   "head_dim": c["D"], "causal": True,
+                   "parallelism": f"shard by (batch, kv-head) over {world} GPU(s), {units} unit(s) on rank 0",
+                   "l2": "256 MiB buffer written between timed steps; inputs 335 MB > 126 MB L2"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms, "api": "fa2.kernel.attention (ctypes -> C ABI fa2_fwd_sm100)"},
+        "roofline": {"bound": "tensor", "achieved": per_gpu_achieved, "peak": peak, "unit": UNIT,
+                     "frac": per_gpu_achieved / peak, "peak_source": peak_src,
+                     "traffic": profile_traffic(),
+                     "algorithmic": f"{rank_flops:.4e} FLOP per launch (4*Hq*D*N(N+1)/2 over the rank's units)"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "ms_samples": {"min": min(ms), "median": statistics.median(ms), "max": max(ms)},
+        "reference_published": {"h100_triton_bf16_n8192_b1_tflops": 447.1,
+                                "source": "reference bench/results/2026-10-04/bench-bf16.log"},
+    }
+    if allgather_ms is not None:
+        line["replicated_out_allgather_ms"] = allgather_ms
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--replicate-out", action="store_true", help="also time the NCCL all-gather of O")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        ap.error("--warmup must be >= 3")
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+    return run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -72,6 +72,11 @@ typedef struct Fa2FwdParams {
   int32_t* err_flag; /* optional device int32; a kernel that gives up on a wait ORs
                         FA2_ERR_TIMEOUT into it. NULL: no report. */
   int64_t timeout_cycles; /* per-wait limit in SM clocks; <= 0 selects the default (~1 s) */
+  const int32_t* gate;     /* optional device int32 start gate: the kernel issues its first
+                              load only once *gate != 0 (set by an upstream kernel or a copy
+                              on another stream). The wait is bounded by timeout_cycles; when
+                              it expires the kernel writes FA2_ERR_TIMEOUT to err_flag and
+                              returns without touching o. NULL: start at once. */
 } Fa2FwdParams;
 
 /* Host-only validation of `p` (no CUDA calls). Replaces the asserts and ValueErrors of

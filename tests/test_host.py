@@ -1,0 +1,143 @@
+"""CPU tests of the host side: the C-ABI library loads and exports what include/fa2_sm100.h
+declares, its host-only validation mirrors the reference's asserts/ValueErrors
+(fa2/kernel.py:218-244 of roy6n23/triton-fa2-forward), and the Python wrapper keeps the
+reference's API (should_pack_gqa, _default_config, error messages, no CPU path)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from fa2 import _lib
+from fa2.kernel import _default_config, attention, should_pack_gqa
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "fa2_sm100.h")
+
+
+def header_functions():
+    txt = open(HEADER).read()
+    return set(re.findall(r"FA2_API\s+[\w\s\*]+?\b(fa2_\w+)\s*\(", txt))
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    declared = header_functions()
+    assert declared == set(_lib.EXPORTED)
+    for name in declared:
+        assert hasattr(L, name), name
+
+
+def test_abi_version_and_struct_size():
+    L = _lib.lib()
+    assert L.fa2_sm100_abi_version() == _lib.ABI_VERSION
+    assert L.fa2_sm100_params_size() == ctypes.sizeof(_lib.Fa2FwdParams) == 224
+
+
+def test_config_entry_point():
+    assert _lib.config(128)[:2] == (128, 128)
+    assert _lib.config(64)[:2] == (128, 128)
+    with pytest.raises(_lib.Fa2Error):
+        _lib.config(96)
+    bm, bn, warps, stages = _default_config(128, True)
+    assert (bm, bn) == (128, 128) and warps == 12 and stages >= 2
+    assert _default_config(64, False)[0] == 128
+
+
+def test_strerror_covers_all_codes():
+    for code in range(0, 13):
+        assert _lib.strerror(code) != "unknown fa2_sm100 status"
+    assert _lib.strerror(999) == "unknown fa2_sm100 status"
+
+
+def contiguous_strides(B, H, N, D):
+    return (H * N * D, N * D, D, 1)
+
+
+def params(**kw):
+    B, Hq, Hkv, Nq, Nkv, D = (kw.pop(n, d) for n, d in
+                              (("B", 2), ("Hq", 8), ("Hkv", 2), ("Nq", 100), ("Nkv", 100), ("D", 128)))
+    base = dict(q_ptr=0x1000, k_ptr=0x2000, v_ptr=0x3000, o_ptr=0x4000,
+                q_stride=contiguous_strides(B, Hq, Nq, D), k_stride=contiguous_strides(B, Hkv, Nkv, D),
+                v_stride=contiguous_strides(B, Hkv, Nkv, D), o_stride=contiguous_strides(B, Hq, Nq, D),
+                batch=B, heads_q=Hq, heads_kv=Hkv, seqlen_q=Nq, seqlen_kv=Nkv, head_dim=D,
+                dtype=_lib.FA2_DTYPE_BF16, causal=1, pack_gqa=0, qk_scale=0.1275)
+    base.update(kw)
+    return _lib.make_params(**base)
+
+
+def test_check_accepts_valid():
+    assert _lib.check(params()) == _lib.FA2_OK
+    assert _lib.check(params(pack_gqa=1)) == _lib.FA2_OK
+    assert _lib.check(params(causal=0, Nq=23, Nkv=70, D=64)) == _lib.FA2_OK
+    assert _lib.check(params(Nq=0, Nkv=0, causal=0)) == _lib.FA2_ERR_SHAPE  # N_kv must be >= 1
+    assert _lib.check(params(Nq=0, Nkv=5, causal=0)) == _lib.FA2_OK          # empty query is a no-op
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(q_ptr=0), _lib.FA2_ERR_NULL),
+    (dict(o_ptr=0), _lib.FA2_ERR_NULL),
+    (dict(batch=0), _lib.FA2_ERR_SHAPE),
+    (dict(Nq=64, Nkv=100), _lib.FA2_ERR_SHAPE),          # causal needs N_q == N_kv (fa2/kernel.py:225-228)
+    (dict(dtype=7), _lib.FA2_ERR_DTYPE),
+    (dict(D=96), _lib.FA2_ERR_HEAD_DIM),
+    (dict(Hq=6, Hkv=4), _lib.FA2_ERR_GQA),                # fa2/kernel.py:223
+    (dict(Hq=6, Hkv=2, pack_gqa=1), _lib.FA2_ERR_PACK),   # group 3 does not divide 128
+    (dict(qk_scale=-0.1), _lib.FA2_ERR_SCALE),            # fa2/kernel.py:242-243
+    (dict(qk_scale=float("nan")), _lib.FA2_ERR_SCALE),
+    (dict(q_stride=(8 * 100 * 128, 100 * 128, 128, 2)), _lib.FA2_ERR_LAYOUT),  # d stride != 1
+    (dict(k_stride=(2 * 100 * 130, 100 * 130, 130, 1)), _lib.FA2_ERR_LAYOUT),  # 260-byte rows
+    (dict(v_ptr=0x3002), _lib.FA2_ERR_LAYOUT),            # misaligned base
+])
+def test_check_rejects(kw, status):
+    assert _lib.check(params(**kw)) == status
+
+
+def test_should_pack_gqa_follows_tile_efficiency():
+    # the reference's truth table (tests/test_correctness.py:189-198)
+    assert should_pack_gqa(1, 4, 128)
+    assert should_pack_gqa(64, 4, 128)
+    assert not should_pack_gqa(4096, 4, 128)
+    assert not should_pack_gqa(1000, 4, 128)
+    assert not should_pack_gqa(64, 1, 128)
+    assert not should_pack_gqa(64, 3, 128)
+    # config 5 (N=1000, group 8) is not auto-packed; its tests force both modes
+    assert not should_pack_gqa(1000, 8, 128)
+
+
+def cpu_qkv(Hq=4, Hkv=2, N=16, D=64, dtype=torch.float16):
+    g = torch.Generator().manual_seed(0)
+    return (torch.randn(2, Hq, N, D, generator=g).to(dtype), torch.randn(2, Hkv, N, D, generator=g).to(dtype),
+            torch.randn(2, Hkv, N, D, generator=g).to(dtype))
+
+
+def test_sm_scale_must_be_positive():
+    q, k, v = cpu_qkv()
+    with pytest.raises(ValueError, match="sm_scale"):
+        attention(q, k, v, sm_scale=-0.125)
+
+
+def test_pack_gqa_needs_block_m_divisible_by_group():
+    q, k, v = cpu_qkv(Hq=6, Hkv=2)
+    with pytest.raises(ValueError, match="BLOCK_M"):
+        attention(q, k, v, causal=True, pack_gqa=True)
+
+
+def test_reference_asserts_kept():
+    q, k, v = cpu_qkv()
+    with pytest.raises(AssertionError):
+        attention(q, k[:, :, :8], v[:, :, :8], causal=True)       # causal with N_q != N_kv
+    with pytest.raises(AssertionError):
+        attention(q.float(), k.float(), v.float())                 # fp32 is not supported
+    with pytest.raises(AssertionError):
+        attention(*cpu_qkv(D=48))                                  # head_dim not a power of two
+    with pytest.raises(AssertionError):
+        attention(*cpu_qkv(Hq=6, Hkv=4))                           # H_q % H_kv
+
+
+def test_no_cpu_path():
+    """The product path has no CPU fallback: CPU tensors are rejected loudly."""
+    q, k, v = cpu_qkv()
+    with pytest.raises(RuntimeError, match="sm_100"):
+        attention(q, k, v)

@@ -1,0 +1,90 @@
+"""CPU tests of the oracle, pinned to the reference.
+
+1. The tiled mirror matches the full-matrix formula (the reference's own algorithm test,
+   tests/test_correctness.py:51-66 of roy6n23/triton-fa2-forward, same grid).
+2. The oracle reproduces the golden fixtures that tests/golden/make_golden.py produced by
+   running the reference's fa2.reference.naive_attention / blocked_attention.
+3. The reference's own Triton kernel output stored in the fixtures meets the reference's
+   acceptance rule against that ground truth (it is the bar our kernel is held to).
+"""
+
+import glob
+import os
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle.reference import attn_flops, blocked_attention, make_qkv, naive_attention
+
+GOLDEN = sorted(glob.glob(os.path.join(os.path.dirname(__file__), "golden", "*.pt")))
+ATOL_FLOOR = 1e-4  # reference tests/test_correctness.py:31
+
+
+def load(path):
+    return torch.load(path, weights_only=False)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("H_q,H_kv", [(4, 4), (4, 2), (4, 1)])
+@pytest.mark.parametrize("N", [1, 16, 37, 100])
+def test_blocked_matches_naive(causal, H_q, H_kv, N):
+    q, k, v = make_qkv(2, H_q, H_kv, N, N, 32, torch.float64)
+    ref = naive_attention(q, k, v, causal=causal)
+    out = blocked_attention(q, k, v, causal=causal, block_m=32, block_n=16)
+    torch.testing.assert_close(out, ref, atol=1e-5, rtol=1e-5)
+
+
+def test_blocked_noncausal_different_lengths():
+    q, k, v = make_qkv(1, 4, 2, 23, 70, 32, torch.float64)
+    torch.testing.assert_close(blocked_attention(q, k, v, causal=False),
+                               naive_attention(q, k, v, causal=False), atol=1e-5, rtol=1e-5)
+
+
+def test_golden_fixtures_present():
+    names = {os.path.basename(p) for p in GOLDEN}
+    assert "plumbing_fp16_causal_d64.pt" in names
+    assert len(GOLDEN) >= 6
+
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[os.path.basename(p)[:-3] for p in GOLDEN])
+def test_oracle_reproduces_reference_naive(path):
+    g = load(path)
+    ours = naive_attention(g["q"].double(), g["k"].double(), g["v"].double(), causal=g["causal"])
+    # fixtures store the fp64 reference result rounded to fp32
+    torch.testing.assert_close(ours.float(), g["ref_naive"], atol=2e-6, rtol=2e-6)
+
+
+@pytest.mark.parametrize("path", [p for p in GOLDEN if "ref_blocked" in load(p)],
+                         ids=lambda p: os.path.basename(p)[:-3])
+def test_oracle_reproduces_reference_blocked(path):
+    g = load(path)
+    ours = blocked_attention(g["q"].double(), g["k"].double(), g["v"].double(), causal=g["causal"])
+    torch.testing.assert_close(ours.float(), g["ref_blocked"], atol=2e-6, rtol=2e-6)
+
+
+@pytest.mark.parametrize("path", [p for p in GOLDEN if "ref_triton" in load(p)],
+                         ids=lambda p: os.path.basename(p)[:-3])
+def test_reference_kernel_meets_its_bar(path):
+    g = load(path)
+    q, k, v, causal = g["q"], g["k"], g["v"], g["causal"]
+    ref = g["ref_naive"].double()
+    sdpa = F.scaled_dot_product_attention(q.float(), k.float().repeat_interleave(q.shape[1] // k.shape[1], 1),
+                                          v.float().repeat_interleave(q.shape[1] // k.shape[1], 1),
+                                          is_causal=causal).to(q.dtype)
+    e_ref_kernel = (g["ref_triton"].double() - ref).abs().max().item()
+    e_sdpa = (sdpa.double() - ref).abs().max().item()
+    assert e_ref_kernel <= 2 * e_sdpa + ATOL_FLOOR
+
+
+def test_flops_formula():
+    # bench/bench.py:83-87 of the reference: 4 * B * H * pairs * D, pairs = N(N+1)/2 causal
+    assert attn_flops(2, 32, 8192, 8192, 128, True) == pytest.approx(1.0996e12, rel=1e-4)
+    assert attn_flops(2, 32, 16384, 16384, 64, False) == pytest.approx(4.398e12, rel=1e-4)
+    assert attn_flops(1, 2, 256, 256, 64, True) == pytest.approx(1.684e7, rel=1e-3)
+
+
+def test_make_qkv_spikes():
+    _, k, _ = make_qkv(1, 2, 1, 200, 200, 128, torch.float32, spike_frac=0.01)
+    n = int((k.abs() == 8.0).sum())
+    assert n == int(k.numel() * 0.01)

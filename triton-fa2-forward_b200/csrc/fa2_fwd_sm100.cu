@@ -12,7 +12,8 @@
 // band, nothing to its right; fa2/kernel.py:150-175).
 //
 // Warp roles (384 threads, three warpgroups):
-//   warps 0-3   softmax for Q tile 0   (thread = one row = one TMEM lane)
+//   warps 0-3   softmax for Q tile 0   (thread = one row = one TMEM lane; warp w reaches
+//               lane quadrant w % 4, the lanes of its SMSP)
 //   warps 4-7   softmax for Q tile 1
 //   warp  8     tcgen05 MMA issue (one thread) + TMEM allocation
 //   warp  9     TMA producer (one thread)
@@ -53,6 +54,7 @@ constexpr int BN = 128;  // K/V rows per tile
 constexpr int Q_TILES = 2;
 constexpr int NUM_WARPS = 12;
 constexpr int NUM_THREADS = NUM_WARPS * 32;
+constexpr int SOFTMAX_WARPS = 8;
 constexpr int MMA_WARP = 8;
 constexpr int LOAD_WARP = 9;
 constexpr int TMEM_COLS = 512;
@@ -60,7 +62,10 @@ constexpr int REGS_SOFTMAX = 208;
 constexpr int REGS_OTHER = 88;
 constexpr float RESCALE_TH = 8.0f;               // log2 units: P may reach 2^8 before a rescale
 constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
-constexpr uint32_t EMU_PAIR_MASK = 0x2222u;      // pairs 1,5,9,13 of every 16: 25% of exp2 on FMA
+#ifndef FA2_EMU_MASK
+#define FA2_EMU_MASK 0x2222u  // pairs 1,5,9,13 of every 16: 25% of the exp2 on the FMA pipe
+#endif
+constexpr uint32_t EMU_PAIR_MASK = FA2_EMU_MASK;
 
 template <int D>
 struct Cfg {
@@ -77,10 +82,11 @@ struct Cfg {
   static constexpr int B_KV_FULL = 2;               // [S]  K/V tile landed
   static constexpr int B_KV_EMPTY = 2 + STAGES;     // [S]  K/V slot released by the MMAs
   static constexpr int B_S_FULL = 2 + 2 * STAGES;   // [2]  S_t in TMEM
-  static constexpr int B_P_FULL = 4 + 2 * STAGES;   // [2]  P_t in TMEM (and O_t rescaled)
+  static constexpr int B_P_FULL = 4 + 2 * STAGES;   // [2]  P_t columns 0-63 in TMEM (and O_t rescaled)
   static constexpr int B_O_FULL = 6 + 2 * STAGES;   // [2]  last PV of tile t retired
   static constexpr int B_MMA_DONE = 8 + 2 * STAGES; // [1]  every MMA retired (teardown)
-  static constexpr int NUM_BARS = 9 + 2 * STAGES;
+  static constexpr int B_P_LATE = 9 + 2 * STAGES;   // [2]  P_t columns 64-127 in TMEM
+  static constexpr int NUM_BARS = 11 + 2 * STAGES;
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
@@ -93,33 +99,38 @@ struct KArgs {
   int n_q, n_kv, group, pack, hblocks;  // hblocks = H_q / pack
   float qk_scale;
   int* err;
+  const int* gate;
   long long timeout;
 };
 
 // ---------------------------------------------------------------- softmax helpers
 
-// Row max of 128 scores with four independent 3-input max chains.
-__device__ __forceinline__ float row_max128(const uint32_t (&s)[4][32]) {
+// Max of 64 scores (two 32-column chunks) with four independent 3-input max chains.
+__device__ __forceinline__ float row_max64(const uint32_t (&s0)[32], const uint32_t (&s1)[32]) {
   float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-#pragma unroll
-    for (int i = 0; i < 32; i += 8) {
-      m0 = fmax3(m0, __uint_as_float(s[c][i + 0]), __uint_as_float(s[c][i + 1]));
-      m1 = fmax3(m1, __uint_as_float(s[c][i + 2]), __uint_as_float(s[c][i + 3]));
-      m2 = fmax3(m2, __uint_as_float(s[c][i + 4]), __uint_as_float(s[c][i + 5]));
-      m3 = fmax3(m3, __uint_as_float(s[c][i + 6]), __uint_as_float(s[c][i + 7]));
-    }
+  for (int i = 0; i < 32; i += 4) {
+    m0 = fmax3(m0, __uint_as_float(s0[i + 0]), __uint_as_float(s0[i + 1]));
+    m1 = fmax3(m1, __uint_as_float(s0[i + 2]), __uint_as_float(s0[i + 3]));
+    m2 = fmax3(m2, __uint_as_float(s1[i + 0]), __uint_as_float(s1[i + 1]));
+    m3 = fmax3(m3, __uint_as_float(s1[i + 2]), __uint_as_float(s1[i + 3]));
   }
   return fmax3(fmaxf(m0, m1), m2, m3);
 }
 
-// p = exp2(s * scale - m) for 32 scores, packed to 16 words of (lo, hi) halves, and
-// accumulated into two packed fp32 partial sums. EMU: a fixed subset of pairs is computed
-// on the FMA pipe (exp2_poly_x2); the subset depends only on the column index.
+// Scores of columns c0 + i with c0 + i > lim are set to -inf (causal / end-of-sequence mask).
+__device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], int c0, int lim) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (c0 + i > lim) s[i] = __float_as_uint(-INFINITY);
+  }
+}
+
+// p = exp2(s * scale - m) for 32 scores: packed to 16 words of (lo, hi) halves for the PV
+// GEMM, and written back into s as fp32 for the row sum. EMU: a fixed subset of pairs is
+// computed on the FMA pipe (exp2_poly_x2); the subset depends only on the column index.
 template <bool BF16, bool EMU>
-__device__ __forceinline__ void make_p32(const uint32_t (&s)[32], uint64_t sc2, uint64_t nm2,
-                                         uint32_t (&pk)[16], uint64_t& sum_a, uint64_t& sum_b) {
+__device__ __forceinline__ void make_p32(uint32_t (&s)[32], uint64_t sc2, uint64_t nm2, uint32_t (&pk)[16]) {
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
     const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), sc2, nm2);
@@ -132,32 +143,29 @@ __device__ __forceinline__ void make_p32(const uint32_t (&s)[32], uint64_t sc2, 
       p1 = ex2_mufu(x1);
     }
     pk[e] = cvt_pack2<BF16>(p0, p1);
-    if (e & 1) {
-      sum_b = f2_add(sum_b, f2_pack(p0, p1));
-    } else {
-      sum_a = f2_add(sum_a, f2_pack(p0, p1));
-    }
+    s[2 * e] = __float_as_uint(p0);
+    s[2 * e + 1] = __float_as_uint(p1);
   }
 }
 
-// O_t row *= alpha (this thread's TMEM lane), 32 columns at a time.
-template <int D>
-__device__ __forceinline__ void rescale_o_row(uint32_t tO, float alpha) {
+// O row *= alpha for this thread's NCOL columns of O_t (its TMEM lane), 16 at a time.
+template <int NCOL>
+__device__ __forceinline__ void rescale_o_cols(uint32_t tO, float alpha) {
   const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
-  for (int c = 0; c < D / 32; ++c) {
-    uint32_t o[32];
-    tmem_ld32(tO + c * 32, o);
+  for (int c = 0; c < NCOL / 16; ++c) {
+    uint32_t o[16];
+    tmem_ld16(tO + c * 16, o);
     tmem_wait_ld();
-    reg_fence32(o);
+    reg_fence16(o);
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      float a, b;
-      f2_unpack(f2_mul(f2_pack(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), a2), a, b);
-      o[i] = __float_as_uint(a);
-      o[i + 1] = __float_as_uint(b);
+    for (int i = 0; i < 16; i += 2) {
+      float x, y;
+      f2_unpack(f2_mul(f2_pack(__uint_as_float(o[i]), __uint_as_float(o[i + 1])), a2), x, y);
+      o[i] = __float_as_uint(x);
+      o[i + 1] = __float_as_uint(y);
     }
-    tmem_st32(tO + c * 32, o);
+    tmem_st16(tO + c * 16, o);
   }
   tmem_wait_st();
 }
@@ -201,6 +209,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(C::B_S_FULL + t), 1);
       mbar_init(bar(C::B_P_FULL + t), BM);
+      mbar_init(bar(C::B_P_LATE + t), BM);
       mbar_init(bar(C::B_O_FULL + t), 1);
     }
     mbar_init(bar(C::B_MMA_DONE), 1);
@@ -240,9 +249,15 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                       c * 64, h, pos, b, pol_q);
         }
       };
-      load_q(0);
+      // Optional start gate: no load is issued before *gate != 0 (bounded like every wait).
+      bool q0_issued = false;
+      if (a.gate != nullptr) ok = flag_wait(a.gate, a.timeout, a.err);
+      if (ok) {
+        load_q(0);
+        q0_issued = true;
+      }
       int issued = 0;
-      for (int i = 0; i < 2 * J; ++i) {
+      for (int i = 0; ok && i < 2 * J; ++i) {
         const int st = i % C::STAGES;
         const uint32_t ph = static_cast<uint32_t>(i / C::STAGES) & 1u;
         if (!mbar_wait(bar(C::B_KV_EMPTY + st), ph ^ 1u, a.timeout, a.err)) {
@@ -263,10 +278,10 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       // can exit, also when another role gave up early.
       for (int i = max(0, issued - C::STAGES); i < issued; ++i) {
         mbar_wait(bar(C::B_KV_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
-                  a.timeout, nullptr);
+                  DEFAULT_TIMEOUT, nullptr);
       }
-      mbar_wait(bar(C::B_Q + 0), 0, a.timeout, nullptr);
-      if (issued > 0) mbar_wait(bar(C::B_Q + 1), 0, a.timeout, nullptr);
+      if (q0_issued) mbar_wait(bar(C::B_Q + 0), 0, DEFAULT_TIMEOUT, nullptr);
+      if (issued > 0) mbar_wait(bar(C::B_Q + 1), 0, DEFAULT_TIMEOUT, nullptr);
     }
   } else if (warp == MMA_WARP) {
     reg_dealloc<REGS_OTHER>();
@@ -274,24 +289,38 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
       constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, true);
+      // Descriptors of the tile bases; a byte offset o inside shared memory adds o >> 4 to
+      // the 14-bit start-address field (addresses stay below 256 KiB, so it never carries).
+      const uint64_t dq_base = sdesc_sw128(sbase + C::OFF_Q, 16, 1024);
+      const uint64_t dk_base = sdesc_sw128(sbase + C::OFF_KV, 16, 1024);
+      const uint64_t dv_base = sdesc_sw128(sbase + C::OFF_KV, C::CHUNK_BYTES, 1024);
       auto issue_qk = [&](int t, int st) {
-        const uint32_t qa = sbase + C::OFF_Q + t * C::TILE_BYTES;
-        const uint32_t ka = sbase + C::OFF_KV + st * C::TILE_BYTES;
+        const uint64_t qd = dq_base + static_cast<uint64_t>((t * C::TILE_BYTES) >> 4);
+        const uint64_t kd = dk_base + static_cast<uint64_t>((st * C::TILE_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::CHUNK_BYTES + (kk & 3) * 32;
-          mma_ss(tmem + t * BN, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(ka + off, 16, 1024),
-                 idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * C::CHUNK_BYTES + (kk & 3) * 32) >> 4);
+          mma_ss(tmem + t * BN, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_pv = [&](int t, int st, bool acc) {
-        const uint32_t va = sbase + C::OFF_KV + st * C::TILE_BYTES;
+      auto issue_pv = [&](int t, int st, bool acc, int kk0, int kk1) {
+        const uint64_t vd = dv_base + static_cast<uint64_t>((st * C::TILE_BYTES) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
+        for (int kk = kk0; kk < kk1; ++kk) {
           mma_ts(tmem + C::TMEM_O + t * D, tmem + t * BN + BN / 2 + kk * 8,
-                 sdesc_sw128(va + kk * 16 * 128, C::CHUNK_BYTES, 1024), idesc_pv,
-                 (acc || kk > 0) ? 1u : 0u);
+                 vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
+      };
+      // PV of tile t in two halves: k-steps 0-3 read P columns 0-63, which the softmax
+      // warps hand over before computing columns 64-127 (k-steps 4-7).
+      auto pv_tile = [&](int t, int st, bool acc, uint32_t pph) -> bool {
+        if (!mbar_wait(bar(C::B_P_FULL + t), pph, a.timeout, a.err)) return false;
+        tc_fence_after();
+        issue_pv(t, st, acc, 0, BN / 32);
+        if (!mbar_wait(bar(C::B_P_LATE + t), pph, a.timeout, a.err)) return false;
+        tc_fence_after();
+        issue_pv(t, st, acc, BN / 32, BN / 16);
+        return true;
       };
       auto kv_wait = [&](int i) -> bool {
         return mbar_wait(bar(C::B_KV_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
@@ -312,9 +341,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           const int sv = iv % C::STAGES, sk = ik % C::STAGES;
           const bool more = (j + 1 < J);
           const uint32_t pph = static_cast<uint32_t>(j) & 1u;
-          if (!kv_wait(iv) || !mbar_wait(bar(C::B_P_FULL + 0), pph, a.timeout, a.err)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(0, sv, j > 0);
+          if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
           if (more) {
             if (!kv_wait(ik)) { ok = false; break; }
             tc_fence_after();
@@ -323,9 +350,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           } else {
             mma_commit(bar(C::B_O_FULL + 0));
           }
-          if (!mbar_wait(bar(C::B_P_FULL + 1), pph, a.timeout, a.err)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(1, sv, j > 0);
+          if (!pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
           mma_commit(bar(C::B_KV_EMPTY + sv));
           if (more) {
             issue_qk(1, sk);
@@ -338,9 +363,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       } while (false);
       // Every issued MMA must retire before TMEM is released.
       mma_commit(bar(C::B_MMA_DONE));
-      mbar_wait(bar(C::B_MMA_DONE), 0, a.timeout, nullptr);
+      mbar_wait(bar(C::B_MMA_DONE), 0, DEFAULT_TIMEOUT, nullptr);
     }
-  } else if (warp < 8) {
+  } else if (warp < SOFTMAX_WARPS) {
     reg_alloc<REGS_SOFTMAX>();
     // ------------------------------------------------------------------ softmax
     const int t = warp >> 2;          // Q tile
@@ -362,29 +387,35 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(j) & 1u, a.timeout, a.err);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
-      uint32_t s[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
-
       const int col0 = j * BN;
       const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
       const bool need_pad = (col0 + BN > a.n_kv);
       const bool masked = need_causal || need_pad;  // uniform over the warpgroup
+      int lim = a.n_kv - 1 - col0;                  // last visible column of this tile, relative
+      if (CAUSAL) lim = min(lim, pos - col0);
+
+      // S row in two halves: the max of the first half overlaps the second half's load.
+      uint32_t s[4][32];
+      tmem_ld32(tS + 0, s[0]);
+      tmem_ld32(tS + 32, s[1]);
+      tmem_wait_ld();
+      reg_fence32(s[0]);
+      reg_fence32(s[1]);
+      tmem_ld32(tS + 64, s[2]);
+      tmem_ld32(tS + 96, s[3]);
       if (masked) {
-        int lim = a.n_kv - 1 - col0;  // last visible column of this tile, relative
-        if (CAUSAL) lim = min(lim, pos - col0);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (c * 32 + i > lim) s[c][i] = __float_as_uint(-INFINITY);
-          }
-        }
+        mask_chunk(s[0], 0, lim);
+        mask_chunk(s[1], 32, lim);
       }
-      const float m_cand = row_max128(s) * qk_scale;
+      const float mx01 = row_max64(s[0], s[1]);
+      tmem_wait_ld();
+      reg_fence32(s[2]);
+      reg_fence32(s[3]);
+      if (masked) {
+        mask_chunk(s[2], 64, lim);
+        mask_chunk(s[3], 96, lim);
+      }
+      const float m_cand = fmaxf(mx01, row_max64(s[2], s[3])) * qk_scale;
       const bool bump = m_cand > m_use + RESCALE_TH;  // first tile: always (m_use = -inf)
       float alpha = 1.0f;
       if (bump) {
@@ -393,29 +424,45 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       }
       if (j > 0 && __any_sync(0xffffffffu, bump)) {
         // PV(t, j-1) has retired: S_t(j) was committed after it.
-        rescale_o_row<D>(tO, alpha);
+        rescale_o_cols<D>(tO, alpha);
       }
-      l *= alpha;
 
+      // P = exp2(s * qk_scale - m) into TMEM; columns 0-63 are handed to the MMA warp
+      // before 64-127 are computed, so PV can start on them.
       const uint64_t nm2 = f2_pack(-m_use, -m_use);
-      uint64_t sum_a = f2_pack(0.0f, 0.0f), sum_b = f2_pack(0.0f, 0.0f);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
         if (masked) {
-          make_p32<BF16, false>(s[c], sc2, nm2, pk, sum_a, sum_b);
+          make_p32<BF16, false>(s[c], sc2, nm2, pk);
         } else {
-          make_p32<BF16, true>(s[c], sc2, nm2, pk, sum_a, sum_b);
+          make_p32<BF16, true>(s[c], sc2, nm2, pk);
         }
         tmem_st16(tP + c * 16, pk);
+        if (c == 1) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(C::B_P_FULL + t));
+        }
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(C::B_P_FULL + t));
-      float sa0, sa1, sb0, sb1;
-      f2_unpack(sum_a, sa0, sa1);
-      f2_unpack(sum_b, sb0, sb1);
-      l += (sa0 + sa1) + (sb0 + sb1);
+      mbar_arrive(bar(C::B_P_LATE + t));
+
+      // Row sum of the fp32 p (before rounding, as fa2/kernel.py:98), off the critical path.
+      uint64_t acc2[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          acc2[(i >> 1) & 3] =
+              f2_add(acc2[(i >> 1) & 3], f2_pack(__uint_as_float(s[c][i]), __uint_as_float(s[c][i + 1])));
+        }
+      }
+      const uint64_t acc01 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
+      float sl0, sl1;
+      f2_unpack(acc01, sl0, sl1);
+      l = l * alpha + (sl0 + sl1);
     }
 
     // ---------------------------------------------------------------- epilogue
@@ -571,6 +618,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.hblocks = p->heads_q / pack;
   ka.qk_scale = p->qk_scale;
   ka.err = p->err_flag;
+  ka.gate = p->gate;
   ka.timeout = p->timeout_cycles > 0 ? p->timeout_cycles : fa2::DEFAULT_TIMEOUT;
 
   const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;

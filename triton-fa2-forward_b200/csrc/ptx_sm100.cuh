@@ -60,6 +60,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long lo
   }
 }
 
+// Waits until the device word *flag becomes non-zero (written by another kernel or the
+// host), bounded like mbar_wait.
+__device__ __forceinline__ bool flag_wait(const int* flag, long long timeout_cycles, const int* err) {
+  const volatile int* f = reinterpret_cast<const volatile int*>(flag);
+  if (*f != 0) return true;
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(256);
+    if (*f != 0) return true;
+    if ((it & 15u) == 0u) {
+      if (clock64() - t0 > timeout_cycles) return false;
+      if (err != nullptr && *reinterpret_cast<const volatile int*>(err) != 0) return false;
+    }
+  }
+}
+
 // ----------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -98,6 +114,21 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// Named barrier over `count` threads that also ANDs a predicate across them: every
+// participant gets true only if all passed true. Orders shared-memory accesses like bar.sync.
+__device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
 }
 
 // Warpgroup register re-balancing (all four warps of a warpgroup execute the same one).
@@ -174,6 +205,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : FA2_R8(0), FA2_R8(8)
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -198,6 +237,9 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
                   "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7])
 __device__ __forceinline__ void reg_fence32(uint32_t (&r)[32]) {
   asm volatile("" : FA2_W8(0), FA2_W8(8), FA2_W8(16), FA2_W8(24) : : "memory");
+}
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
+  asm volatile("" : FA2_W8(0), FA2_W8(8) : : "memory");
 }
 #undef FA2_W8
 

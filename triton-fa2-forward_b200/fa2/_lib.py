@@ -64,6 +64,7 @@ class Fa2FwdParams(ctypes.Structure):
         ("qk_scale", ctypes.c_float),
         ("err_flag", ctypes.c_void_p),
         ("timeout_cycles", ctypes.c_int64),
+        ("gate", ctypes.c_void_p),
     ]
 
 
@@ -128,7 +129,7 @@ def config(head_dim):
 
 def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stride,
                 batch, heads_q, heads_kv, seqlen_q, seqlen_kv, head_dim, dtype, causal,
-                pack_gqa, qk_scale, err_flag=0, timeout_cycles=0):
+                pack_gqa, qk_scale, err_flag=0, timeout_cycles=0, gate=0):
     p = Fa2FwdParams()
     p.q, p.k, p.v, p.o = q_ptr, k_ptr, v_ptr, o_ptr
     p.q_stride[:] = list(q_stride)
@@ -141,6 +142,7 @@ def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stri
     p.qk_scale = float(qk_scale)
     p.err_flag = err_flag or None
     p.timeout_cycles = int(timeout_cycles)
+    p.gate = gate or None
     return p
 
 

@@ -1,0 +1,51 @@
+"""Profiling target: a few warm-up launches of the FA2 forward on one config, then the
+launch(es) a profiler captures (e.g. `ncu -k regex:fa2_fwd -s <warmup> -c 1`).
+Mirrors the role of the reference's bench/profile_target.py.
+
+    python triton-fa2-forward_b200/profile_target.py [--config headline] [--warmup 2] [--launches 1]
+
+Configs are the BASELINE.json shapes; inputs are seeded N(0,1) generated on the device.
+The headline config holds 470 MB (inputs 335 MB > 126 MB L2), so DRAM counters are meaningful.
+"""
+
+import argparse
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+import torch  # noqa: E402
+
+from fa2.kernel import attention, check_device_errors  # noqa: E402
+
+CONFIGS = {
+    "plumbing": (1, 2, 2, 256, 64, torch.float16, True, 1.0),
+    "mha_causal": (4, 16, 16, 4096, 128, torch.bfloat16, True, 1.0),
+    "headline": (2, 32, 8, 8192, 128, torch.bfloat16, True, 1.0),
+    "full_long": (2, 32, 32, 16384, 64, torch.float16, False, 0.5),
+    "pack_tail": (16, 64, 8, 1000, 128, torch.bfloat16, True, 1.0),
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", choices=list(CONFIGS), default="headline")
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--launches", type=int, default=1)
+    ap.add_argument("--pack", choices=["auto", "on", "off"], default="auto")
+    args = ap.parse_args()
+    B, Hq, Hkv, N, D, dt, causal, scale = CONFIGS[args.config]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, Hq, N, D, device="cuda", dtype=dt, generator=g) * scale
+    k = torch.randn(B, Hkv, N, D, device="cuda", dtype=dt, generator=g) * scale
+    v = torch.randn(B, Hkv, N, D, device="cuda", dtype=dt, generator=g) * scale
+    pack = {"auto": None, "on": True, "off": False}[args.pack]
+    for _ in range(args.warmup + args.launches):
+        attention(q, k, v, causal=causal, pack_gqa=pack)
+    torch.cuda.synchronize()
+    check_device_errors()
+    print(f"ok: {args.config} x{args.warmup + args.launches}")
+
+
+if __name__ == "__main__":
+    main()
