@@ -65,7 +65,15 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_EMU_MASK
 #define FA2_EMU_MASK 0x2222u  // pairs 1,5,9,13 of every 16: 25% of the exp2 on the FMA pipe
 #endif
+#ifndef FA2_P_SPLIT
+#define FA2_P_SPLIT 3  // P chunks (of 32 columns) handed to the MMA warp before the rest
+#endif
+#ifndef FA2_MMA_SPIN
+#define FA2_MMA_SPIN 0  // 1: the MMA thread polls its barriers without suspending (measured: no gain)
+#endif
 constexpr uint32_t EMU_PAIR_MASK = FA2_EMU_MASK;
+constexpr int P_SPLIT = FA2_P_SPLIT;
+static_assert(P_SPLIT >= 1 && P_SPLIT <= 3, "P hand-off split");
 
 template <int D>
 struct Cfg {
@@ -82,10 +90,10 @@ struct Cfg {
   static constexpr int B_KV_FULL = 2;               // [S]  K/V tile landed
   static constexpr int B_KV_EMPTY = 2 + STAGES;     // [S]  K/V slot released by the MMAs
   static constexpr int B_S_FULL = 2 + 2 * STAGES;   // [2]  S_t in TMEM
-  static constexpr int B_P_FULL = 4 + 2 * STAGES;   // [2]  P_t columns 0-63 in TMEM (and O_t rescaled)
+  static constexpr int B_P_FULL = 4 + 2 * STAGES;   // [2]  P_t columns [0, 32*P_SPLIT) in TMEM, O_t rescaled
   static constexpr int B_O_FULL = 6 + 2 * STAGES;   // [2]  last PV of tile t retired
   static constexpr int B_MMA_DONE = 8 + 2 * STAGES; // [1]  every MMA retired (teardown)
-  static constexpr int B_P_LATE = 9 + 2 * STAGES;   // [2]  P_t columns 64-127 in TMEM
+  static constexpr int B_P_LATE = 9 + 2 * STAGES;   // [2]  the remaining P_t columns in TMEM
   static constexpr int NUM_BARS = 11 + 2 * STAGES;
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
@@ -311,27 +319,30 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                  vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
       };
-      // PV of tile t in two halves: k-steps 0-3 read P columns 0-63, which the softmax
-      // warps hand over before computing columns 64-127 (k-steps 4-7).
+      auto mwait = [&](int b_idx, uint32_t parity) -> bool {
+        return FA2_MMA_SPIN ? mbar_wait_spin(bar(b_idx), parity, a.timeout, a.err)
+                            : mbar_wait(bar(b_idx), parity, a.timeout, a.err);
+      };
+      // PV of tile t in two parts: the k-steps reading P columns [0, 32 * P_SPLIT), which
+      // the softmax warps hand over before computing the rest, then the remaining k-steps.
       auto pv_tile = [&](int t, int st, bool acc, uint32_t pph) -> bool {
-        if (!mbar_wait(bar(C::B_P_FULL + t), pph, a.timeout, a.err)) return false;
+        if (!mwait(C::B_P_FULL + t, pph)) return false;
         tc_fence_after();
-        issue_pv(t, st, acc, 0, BN / 32);
-        if (!mbar_wait(bar(C::B_P_LATE + t), pph, a.timeout, a.err)) return false;
+        issue_pv(t, st, acc, 0, 2 * P_SPLIT);
+        if (!mwait(C::B_P_LATE + t, pph)) return false;
         tc_fence_after();
-        issue_pv(t, st, acc, BN / 32, BN / 16);
+        issue_pv(t, st, acc, 2 * P_SPLIT, BN / 16);
         return true;
       };
       auto kv_wait = [&](int i) -> bool {
-        return mbar_wait(bar(C::B_KV_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
-                         a.timeout, a.err);
+        return mwait(C::B_KV_FULL + i % C::STAGES, static_cast<uint32_t>(i / C::STAGES) & 1u);
       };
       do {
-        if (!mbar_wait(bar(C::B_Q + 0), 0, a.timeout, a.err) || !kv_wait(0)) { ok = false; break; }
+        if (!mwait(C::B_Q + 0, 0) || !kv_wait(0)) { ok = false; break; }
         tc_fence_after();
         issue_qk(0, 0);
         mma_commit(bar(C::B_S_FULL + 0));
-        if (!mbar_wait(bar(C::B_Q + 1), 0, a.timeout, a.err)) { ok = false; break; }
+        if (!mwait(C::B_Q + 1, 0)) { ok = false; break; }
         tc_fence_after();
         issue_qk(1, 0);
         mma_commit(bar(C::B_S_FULL + 1));
@@ -394,28 +405,18 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       int lim = a.n_kv - 1 - col0;                  // last visible column of this tile, relative
       if (CAUSAL) lim = min(lim, pos - col0);
 
-      // S row in two halves: the max of the first half overlaps the second half's load.
+      // The whole S row (128 columns) in one batch of loads and a single wait.
       uint32_t s[4][32];
-      tmem_ld32(tS + 0, s[0]);
-      tmem_ld32(tS + 32, s[1]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
       tmem_wait_ld();
-      reg_fence32(s[0]);
-      reg_fence32(s[1]);
-      tmem_ld32(tS + 64, s[2]);
-      tmem_ld32(tS + 96, s[3]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
       if (masked) {
-        mask_chunk(s[0], 0, lim);
-        mask_chunk(s[1], 32, lim);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) mask_chunk(s[c], c * 32, lim);
       }
-      const float mx01 = row_max64(s[0], s[1]);
-      tmem_wait_ld();
-      reg_fence32(s[2]);
-      reg_fence32(s[3]);
-      if (masked) {
-        mask_chunk(s[2], 64, lim);
-        mask_chunk(s[3], 96, lim);
-      }
-      const float m_cand = fmaxf(mx01, row_max64(s[2], s[3])) * qk_scale;
+      const float m_cand = fmaxf(row_max64(s[0], s[1]), row_max64(s[2], s[3])) * qk_scale;
       const bool bump = m_cand > m_use + RESCALE_TH;  // first tile: always (m_use = -inf)
       float alpha = 1.0f;
       if (bump) {
@@ -427,8 +428,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         rescale_o_cols<D>(tO, alpha);
       }
 
-      // P = exp2(s * qk_scale - m) into TMEM; columns 0-63 are handed to the MMA warp
-      // before 64-127 are computed, so PV can start on them.
+      // P = exp2(s * qk_scale - m) into TMEM; the first P_SPLIT chunks are handed to the
+      // MMA warp before the rest are computed, so PV can start on them.
       const uint64_t nm2 = f2_pack(-m_use, -m_use);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -439,7 +440,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           make_p32<BF16, true>(s[c], sc2, nm2, pk);
         }
         tmem_st16(tP + c * 16, pk);
-        if (c == 1) {
+        if (c == P_SPLIT - 1) {
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(bar(C::B_P_FULL + t));

@@ -44,6 +44,33 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that polls without suspending the thread (lowest wake-up latency; for the
+// single MMA-issuing thread, whose waits sit on the critical path).
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, long long timeout_cycles,
+                                               const int* err) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u) {
+      if (clock64() - t0 > timeout_cycles) return false;
+      if (err != nullptr && *reinterpret_cast<const volatile int*>(err) != 0) return false;
+    }
+  }
+}
+
 // Waits for the phase of `bar` with the given parity to complete. Gives up after
 // `timeout_cycles` SM clocks, or as soon as another CTA has raised the kernel's error
 // word, and returns false; the caller then abandons its role and joins the teardown.
