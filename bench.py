@@ -151,8 +151,7 @@ def cpu_baseline_sample(seconds=12.0, threads=None):
     sys.path.insert(0, REPO)
     from oracle.reference import naive_attention
 
-    if threads:
-        torch.set_num_threads(threads)
+    torch.set_num_threads(threads or os.cpu_count() or 1)
     c = HEADLINE
     G = c["Hq"] // c["Hkv"]
     g = torch.Generator().manual_seed(1)
@@ -181,6 +180,8 @@ def run_reference(args, world, rank):
     sys.path.insert(0, REPO)
     from oracle.reference import naive_attention
 
+    # torchrun sets OMP_NUM_THREADS=1 per rank; the CPU baseline uses every host core.
+    torch.set_num_threads(os.cpu_count() or 1)
     c = HEADLINE
     G = c["Hq"] // c["Hkv"]
     g = torch.Generator().manual_seed(1)
