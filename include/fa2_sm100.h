@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define FA2_SM100_ABI_VERSION 1
+#define FA2_SM100_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define FA2_API __attribute__((visibility("default")))
@@ -47,7 +47,8 @@ enum Fa2Status {
   FA2_ERR_TMA_ENCODE = 9,    /* cuTensorMapEncodeTiled rejected a descriptor */
   FA2_ERR_LAUNCH = 10,       /* the CUDA launch failed (cudaGetLastError) */
   FA2_ERR_DEVICE = 11,       /* current device is not sm_100 / driver entry point missing */
-  FA2_ERR_TIMEOUT = 12       /* value written to err_flag by a kernel whose bounded wait expired */
+  FA2_ERR_TIMEOUT = 12,      /* value written to err_flag by a kernel whose bounded wait expired */
+  FA2_ERR_WORKSPACE = 13     /* num_splits > 1 without a large enough, 16-byte aligned workspace */
 };
 
 typedef struct Fa2FwdParams {
@@ -77,6 +78,13 @@ typedef struct Fa2FwdParams {
                               on another stream). The wait is bounded by timeout_cycles; when
                               it expires the kernel writes FA2_ERR_TIMEOUT to err_flag and
                               returns without touching o. NULL: start at once. */
+  int32_t num_splits;      /* split-KV: >1 splits every CTA's K/V range into num_splits parts that
+                              run as separate CTAs and are merged by a second kernel (short
+                              queries against long K/V). <= 1: no split, no workspace. */
+  int32_t reserved0;
+  void* workspace;         /* device scratch for num_splits > 1 (fp32 partial O + row
+                              log-sum-exp), at least fa2_fwd_sm100_workspace_bytes() bytes */
+  int64_t workspace_bytes;
 } Fa2FwdParams;
 
 /* Host-only validation of `p` (no CUDA calls). Replaces the asserts and ValueErrors of
@@ -88,6 +96,10 @@ FA2_API int fa2_fwd_sm100_check(const Fa2FwdParams* p);
  * the launch, without synchronising. Replaces `_attn_fwd[grid](...)`
  * (fa2/kernel.py:246-259). */
 FA2_API int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream);
+
+/* Bytes of device workspace fa2_fwd_sm100 needs for `p` (0 when p->num_splits <= 1).
+ * Host only; the reference has no split-KV (its README lists it out of scope). */
+FA2_API int64_t fa2_fwd_sm100_workspace_bytes(const Fa2FwdParams* p);
 
 /* Static description of the compiled kernel family (fa2/kernel.py:186-195 analogue):
  * fills BLOCK_M, BLOCK_N, threads per CTA, K/V pipeline stages and dynamic shared memory

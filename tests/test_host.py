@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_struct_size():
     L = _lib.lib()
     assert L.fa2_sm100_abi_version() == _lib.ABI_VERSION
-    assert L.fa2_sm100_params_size() == ctypes.sizeof(_lib.Fa2FwdParams) == 224
+    assert L.fa2_sm100_params_size() == ctypes.sizeof(_lib.Fa2FwdParams) == 248
 
 
 def test_config_entry_point():
@@ -46,7 +46,7 @@ def test_config_entry_point():
 
 
 def test_strerror_covers_all_codes():
-    for code in range(0, 13):
+    for code in range(0, 14):
         assert _lib.strerror(code) != "unknown fa2_sm100 status"
     assert _lib.strerror(999) == "unknown fa2_sm100 status"
 
@@ -141,3 +141,27 @@ def test_no_cpu_path():
     q, k, v = cpu_qkv()
     with pytest.raises(RuntimeError, match="sm_100"):
         attention(q, k, v)
+
+
+def test_workspace_validation_and_size():
+    p = params(causal=0, Nq=4, Nkv=4096, num_splits=4)
+    need = _lib.workspace_bytes(p)
+    # 4 splits x (B * Hq) row slices x 256 padded rows x (D + 1) fp32 + 256
+    assert need == 4 * (2 * 8) * 256 * 129 * 4 + 256
+    assert _lib.check(p) == _lib.FA2_ERR_WORKSPACE                       # no workspace
+    p2 = params(causal=0, Nq=4, Nkv=4096, num_splits=4, workspace=0x10000, workspace_bytes=need - 1)
+    assert _lib.check(p2) == _lib.FA2_ERR_WORKSPACE                      # too small
+    p3 = params(causal=0, Nq=4, Nkv=4096, num_splits=4, workspace=0x10008, workspace_bytes=need)
+    assert _lib.check(p3) == _lib.FA2_ERR_WORKSPACE                      # misaligned
+    p4 = params(causal=0, Nq=4, Nkv=4096, num_splits=4, workspace=0x10000, workspace_bytes=need)
+    assert _lib.check(p4) == _lib.FA2_OK
+    assert _lib.workspace_bytes(params()) == 0                           # no split, no workspace
+
+
+def test_auto_num_splits():
+    from fa2.kernel import auto_num_splits
+    assert auto_num_splits(2, 32, 8192, 8192, 4, 1, True) == 1          # causal prefill: never
+    assert auto_num_splits(2, 32, 8192, 8192, 4, 1, False) == 1         # GPU already full
+    assert auto_num_splits(16, 32, 1, 4096, 4, 4, False) == 1           # 128 CTAs already ~ one wave
+    assert auto_num_splits(4, 32, 1, 65536, 4, 4, False) == 4           # 32 CTAs -> 128 in one wave
+    assert auto_num_splits(1, 8, 1, 512, 8, 8, False) == 1              # too few K/V tiles

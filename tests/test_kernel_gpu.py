@@ -286,3 +286,43 @@ def test_start_gate_timeout_is_reported():
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     assert torch.equal(out, attention(q, k, v))
+
+
+# ------------------------------------------------------------------------ split-KV
+# Extension beyond the reference (its README lists split-KV out of scope): short queries
+# against long K/V split each CTA's K/V range over several CTAs and merge the fp32 partials.
+@pytest.mark.parametrize("num_splits", [2, 3, 4, 7])
+@pytest.mark.parametrize("causal", [False, True])
+def test_split_kv_parity(num_splits, causal):
+    N = 1000
+    check_against_oracle(*make_cuda_qkv(2, 8, 2, N, N, 128, torch.bfloat16), causal, num_splits=num_splits)
+
+
+@pytest.mark.parametrize("N_q,N_kv", [(1, 4096), (4, 4096), (16, 8192), (1, 1000), (33, 2048)])
+@pytest.mark.parametrize("D", [64, 128])
+def test_split_kv_short_queries(N_q, N_kv, D):
+    q, k, v = make_cuda_qkv(4, 32, 8, N_q, N_kv, D, torch.bfloat16)
+    from fa2.kernel import auto_num_splits
+    assert auto_num_splits(4, 32, N_q, N_kv, 4, 4 if N_q * 4 <= 256 else 1, False) >= 1
+    check_against_oracle(q, k, v, causal=False)                 # auto splits
+    check_against_oracle(q, k, v, causal=False, num_splits=5)   # forced
+
+
+def test_split_kv_more_splits_than_tiles():
+    """Splits past a row block's K/V range are skipped by the kernel and by the merge."""
+    check_against_oracle(*make_cuda_qkv(1, 4, 1, 300, 300, 64, torch.float16), True, num_splits=16)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_split_kv_pack_bit_equal(causal):
+    q, k, v = make_cuda_qkv(2, 32, 4, 700, 700, 128, torch.bfloat16)
+    a = attention(q, k, v, causal=causal, pack_gqa=True, num_splits=3)
+    b = attention(q, k, v, causal=causal, pack_gqa=False, num_splits=3)
+    assert torch.equal(a, b)
+
+
+def test_split_kv_noncontiguous_output_strides():
+    q, k, v = (t.transpose(1, 2).contiguous().transpose(1, 2)
+               for t in make_cuda_qkv(2, 8, 2, 9, 3000, 128, torch.float16))
+    out = check_against_oracle(q, k, v, causal=False, num_splits=4)
+    assert out.stride() == q.stride()

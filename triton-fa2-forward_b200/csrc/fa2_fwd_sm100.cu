@@ -71,6 +71,12 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_MMA_SPIN
 #define FA2_MMA_SPIN 0  // 1: the MMA thread polls its barriers without suspending (measured: no gain)
 #endif
+#ifndef FA2_P_ALL_FIRST
+#define FA2_P_ALL_FIRST 0  // 1: compute all of P before the first TMEM store (else store per chunk)
+#endif
+#ifndef FA2_SEQ_SOFTMAX
+#define FA2_SEQ_SOFTMAX 0  // 1: the two tiles' exp phases take turns instead of overlapping
+#endif
 constexpr uint32_t EMU_PAIR_MASK = FA2_EMU_MASK;
 constexpr int P_SPLIT = FA2_P_SPLIT;
 static_assert(P_SPLIT >= 1 && P_SPLIT <= 3, "P hand-off split");
@@ -94,7 +100,8 @@ struct Cfg {
   static constexpr int B_O_FULL = 6 + 2 * STAGES;   // [2]  last PV of tile t retired
   static constexpr int B_MMA_DONE = 8 + 2 * STAGES; // [1]  every MMA retired (teardown)
   static constexpr int B_P_LATE = 9 + 2 * STAGES;   // [2]  the remaining P_t columns in TMEM
-  static constexpr int NUM_BARS = 11 + 2 * STAGES;
+  static constexpr int B_SEQ = 11 + 2 * STAGES;     // [2]  exp phase of tile t done (turn-taking)
+  static constexpr int NUM_BARS = 13 + 2 * STAGES;
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
@@ -109,7 +116,23 @@ struct KArgs {
   int* err;
   const int* gate;
   long long timeout;
+  // split-KV: CTA (x, y, z) covers K/V tiles [z * split_tiles, (z + 1) * split_tiles) of its
+  // range and writes fp32 O / l plus the row log2-sum-exp to the workspace (num_splits > 1).
+  int num_splits, split_tiles, rows_pad;
+  float* o_part;    // [num_splits][gridDim.x][rows_pad][D]
+  float* lse_part;  // [num_splits][gridDim.x][rows_pad]
 };
+
+// K/V tiles a CTA of 256-row block mb visits (>= 1): its causal band end, or all of N_kv.
+template <bool CAUSAL>
+__host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, int pack) {
+  int kv_end = n_kv;
+  if (CAUSAL) {
+    const int last_pos = min((mb * 256 + 255) / pack, n_q - 1);
+    kv_end = min(last_pos + 1, n_kv);
+  }
+  return (kv_end + 127) / 128;
+}
 
 // ---------------------------------------------------------------- softmax helpers
 
@@ -200,12 +223,14 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   const int hkv = hq0 / a.group;
   const int mb = CAUSAL ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : static_cast<int>(blockIdx.y);
   const int row0 = mb * (Q_TILES * BM);  // first packed row of this CTA
-  int kv_end = a.n_kv;
-  if (CAUSAL) {
-    const int last_pos = min((row0 + Q_TILES * BM - 1) / a.pack, a.n_q - 1);
-    kv_end = min(last_pos + 1, a.n_kv);
+  static_assert(Q_TILES * BM == 256 && BN == 128, "cta_kv_tiles assumes 256-row CTAs, 128-row K/V tiles");
+  const int J_cta = cta_kv_tiles<CAUSAL>(mb, a.n_q, a.n_kv, a.pack);  // K/V tiles of the CTA (>= 1)
+  int j0 = 0, J = J_cta;  // this CTA's share: tiles [j0, j0 + J)
+  if (a.num_splits > 1) {
+    j0 = static_cast<int>(blockIdx.z) * a.split_tiles;
+    J = min(J_cta - j0, a.split_tiles);
+    if (J <= 0) return;  // split past this row block's band: nothing to do (uniform, before any sync)
   }
-  const int J = (kv_end + BN - 1) / BN;  // K/V tiles visited by this CTA (>= 1)
 
   if (warp == LOAD_WARP && lane == 0) {
     mbar_init(bar(C::B_Q + 0), 1);
@@ -218,6 +243,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       mbar_init(bar(C::B_S_FULL + t), 1);
       mbar_init(bar(C::B_P_FULL + t), BM);
       mbar_init(bar(C::B_P_LATE + t), BM);
+      mbar_init(bar(C::B_SEQ + t), BM);
       mbar_init(bar(C::B_O_FULL + t), 1);
     }
     mbar_init(bar(C::B_MMA_DONE), 1);
@@ -277,7 +303,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c) {
           tma_load_4d(sbase + C::OFF_KV + st * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
-                      bar(C::B_KV_FULL + st), c * 64, (i >> 1) * BN, hkv, b, pol_kv);
+                      bar(C::B_KV_FULL + st), c * 64, (j0 + (i >> 1)) * BN, hkv, b, pol_kv);
         }
         ++issued;
         if (i == 0) load_q(1);
@@ -398,7 +424,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(j) & 1u, a.timeout, a.err);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
-      const int col0 = j * BN;
+      const int col0 = (j0 + j) * BN;
       const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
       const bool need_pad = (col0 + BN > a.n_kv);
       const bool masked = need_causal || need_pad;  // uniform over the warpgroup
@@ -430,7 +456,40 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
       // P = exp2(s * qk_scale - m) into TMEM; the first P_SPLIT chunks are handed to the
       // MMA warp before the rest are computed, so PV can start on them.
-      const uint64_t nm2 = f2_pack(-m_use, -m_use);
+      if (FA2_SEQ_SOFTMAX) {
+        // Tile 1 computes step j after tile 0's step j; tile 0 computes step j after tile 1's
+        // step j - 1, so the two exp phases of an SMSP do not compete for its XU / FMA pipes.
+        const bool need = (t == 1) || (j > 0);
+        if (need) {
+          const uint32_t par = static_cast<uint32_t>(t == 1 ? j : j - 1) & 1u;
+          bool w2 = mbar_wait(bar(C::B_SEQ + (t ^ 1)), par, a.timeout, a.err);
+          if (!__all_sync(0xffffffffu, w2)) { ok = false; break; }
+        }
+      }
+      // A row that has seen only masked columns so far (possible inside a split) keeps
+      // m_use = -inf; its p must be exactly 0, not exp2(-inf + inf).
+      const float m_safe = (m_use == -INFINITY) ? 0.0f : m_use;
+      const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
+#if FA2_P_ALL_FIRST
+      uint32_t pk[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (masked) {
+          make_p32<BF16, false>(s[c], sc2, nm2, pk[c]);
+        } else {
+          make_p32<BF16, true>(s[c], sc2, nm2, pk[c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        tmem_st16(tP + c * 16, pk[c]);
+        if (c == P_SPLIT - 1) {
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(C::B_P_FULL + t));
+        }
+      }
+#else
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
@@ -446,9 +505,11 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           mbar_arrive(bar(C::B_P_FULL + t));
         }
       }
+#endif
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(C::B_P_LATE + t));
+      if (FA2_SEQ_SOFTMAX) mbar_arrive(bar(C::B_SEQ + t));
 
       // Row sum of the fp32 p (before rounding, as fa2/kernel.py:98), off the critical path.
       uint64_t acc2[4] = {0, 0, 0, 0};
@@ -471,6 +532,28 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       bool w = mbar_wait(bar(C::B_O_FULL + t), 0, a.timeout, a.err);
       if (!__all_sync(0xffffffffu, w)) ok = false;
     }
+    if (ok && a.num_splits > 1) {
+      // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
+      // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
+      tc_fence_after();
+      const bool has = (l > 0.0f);
+      const float inv_l = has ? 1.0f / l : 0.0f;
+      const int64_t slot = (static_cast<int64_t>(blockIdx.z) * gridDim.x + blockIdx.x) * a.rows_pad + tile_row0 + r;
+      float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          dst[c * 8 + v] = make_float4(__uint_as_float(o[4 * v]) * inv_l, __uint_as_float(o[4 * v + 1]) * inv_l,
+                                       __uint_as_float(o[4 * v + 2]) * inv_l, __uint_as_float(o[4 * v + 3]) * inv_l);
+        }
+      }
+      a.lse_part[slot] = has ? m_use + log2f(l) : -INFINITY;
+    } else
     if (ok) {
       tc_fence_after();
       const float inv_l = 1.0f / l;
@@ -526,6 +609,54 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   }
 }
 
+// --------------------------------------------------------------- split-KV combine
+// One warp per packed row: O = sum_s w_s O_s / sum_s w_s with w_s = 2^(lse_s - max lse), over
+// the splits that cover this row's 256-row block, written in the input dtype with o's strides.
+struct CombineArgs {
+  int n_q, n_kv, pack, hblocks, rows_pad, num_splits, split_tiles;
+  int64_t ob, oh, on;  // output element strides (b, h, n); d stride is 1
+};
+
+template <int D, bool CAUSAL, bool BF16>
+__global__ void __launch_bounds__(256)
+fa2_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse_part, void* out,
+                   const CombineArgs c) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int R = blockIdx.x * 8 + warp;  // packed row within the (batch, head block) slice
+  if (R >= c.n_q * c.pack) return;
+  const int x = blockIdx.y;
+  const int b = x / c.hblocks;
+  const int h = (x % c.hblocks) * c.pack + R % c.pack;
+  const int pos = R / c.pack;
+  const int J_cta = cta_kv_tiles<CAUSAL>(R / 256, c.n_q, c.n_kv, c.pack);
+  const int ns = min(c.num_splits, (J_cta + c.split_tiles - 1) / c.split_tiles);
+  const int64_t xs = static_cast<int64_t>(gridDim.y);
+  float mx = -INFINITY;
+  for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, lse_part[(sp * xs + x) * c.rows_pad + R]);
+  constexpr int PER = D / 32;  // columns per lane
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.0f;
+  float wsum = 0.0f;
+  for (int sp = 0; sp < ns; ++sp) {
+    const int64_t slot = (sp * xs + x) * c.rows_pad + R;
+    const float lse = lse_part[slot];
+    if (lse == -INFINITY) continue;  // this split saw no visible column of the row
+    const float w = exp2f(lse - mx);
+    wsum += w;
+    const float* src = o_part + slot * D + lane * PER;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) acc[i] = fmaf(w, src[i], acc[i]);
+  }
+  const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+  uint16_t* dst = reinterpret_cast<uint16_t*>(out) + b * c.ob + h * c.oh + pos * c.on + lane * PER;
+#pragma unroll
+  for (int i = 0; i < PER; i += 2) {
+    const uint32_t pk = cvt_pack2<BF16>(acc[i] * inv, acc[i + 1] * inv);
+    *reinterpret_cast<uint32_t*>(dst + i) = pk;
+  }
+}
+
 }  // namespace fa2
 
 // =============================================================================== host
@@ -575,6 +706,27 @@ bool make_map(CUtensorMap* m, bool bf16, const void* base, const int64_t dims[4]
 
 constexpr int kMaxDevices = 64;
 
+struct SplitPlan {
+  int num_splits = 1, split_tiles = 0, rows_pad = 0, xblocks = 0;
+  int64_t bytes = 0;
+};
+
+SplitPlan plan_splits(const Fa2FwdParams* p) {
+  SplitPlan sp;
+  if (p->num_splits <= 1) return sp;
+  const int group = p->heads_q / p->heads_kv;
+  const int pack = p->pack_gqa ? group : 1;
+  const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
+  const int mblocks = static_cast<int>((rows + 255) / 256);
+  const int j_max = (p->seqlen_kv + 127) / 128;
+  sp.num_splits = p->num_splits;
+  sp.split_tiles = (j_max + p->num_splits - 1) / p->num_splits;
+  sp.rows_pad = mblocks * 256;
+  sp.xblocks = p->batch * (p->heads_q / pack);
+  sp.bytes = static_cast<int64_t>(sp.num_splits) * sp.xblocks * sp.rows_pad * (p->head_dim + 1) * 4 + 256;
+  return sp;
+}
+
 template <int D, bool CAUSAL, bool BF16>
 int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   using C = Cfg<D>;
@@ -621,12 +773,41 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.err = p->err_flag;
   ka.gate = p->gate;
   ka.timeout = p->timeout_cycles > 0 ? p->timeout_cycles : fa2::DEFAULT_TIMEOUT;
+  const SplitPlan sp = plan_splits(p);
+  ka.num_splits = sp.num_splits;
+  ka.split_tiles = sp.split_tiles;
+  ka.rows_pad = sp.rows_pad;
+  ka.o_part = nullptr;
+  ka.lse_part = nullptr;
+  if (sp.num_splits > 1) {
+    // workspace: [splits][x][rows_pad][D] fp32 partial O, then [splits][x][rows_pad] lse
+    uint8_t* ws = static_cast<uint8_t*>(p->workspace);
+    ka.o_part = reinterpret_cast<float*>(ws);
+    ka.lse_part = reinterpret_cast<float*>(ws + static_cast<int64_t>(sp.num_splits) * sp.xblocks * sp.rows_pad * D * 4);
+  }
 
   const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(p->batch) * ka.hblocks),
-                  static_cast<unsigned>((rows + fa2::Q_TILES * fa2::BM - 1) / (fa2::Q_TILES * fa2::BM)));
+                  static_cast<unsigned>((rows + fa2::Q_TILES * fa2::BM - 1) / (fa2::Q_TILES * fa2::BM)),
+                  static_cast<unsigned>(sp.num_splits));
   kern<<<grid, fa2::NUM_THREADS, C::SMEM_ALLOC, stream>>>(tmQ, tmK, tmV, tmO, ka);
   if (cudaGetLastError() != cudaSuccess) return FA2_ERR_LAUNCH;
+  if (sp.num_splits > 1) {
+    fa2::CombineArgs ca;
+    ca.n_q = p->seqlen_q;
+    ca.n_kv = p->seqlen_kv;
+    ca.pack = pack;
+    ca.hblocks = ka.hblocks;
+    ca.rows_pad = sp.rows_pad;
+    ca.num_splits = sp.num_splits;
+    ca.split_tiles = sp.split_tiles;
+    ca.ob = p->o_stride[0];
+    ca.oh = p->o_stride[1];
+    ca.on = p->o_stride[2];
+    const dim3 cgrid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(sp.xblocks));
+    fa2::fa2_combine_kernel<D, CAUSAL, BF16><<<cgrid, 256, 0, stream>>>(ka.o_part, ka.lse_part, p->o, ca);
+    if (cudaGetLastError() != cudaSuccess) return FA2_ERR_LAUNCH;
+  }
   return FA2_OK;
 }
 
@@ -656,6 +837,7 @@ extern "C" {
 
 int fa2_sm100_abi_version(void) { return FA2_SM100_ABI_VERSION; }
 
+
 int64_t fa2_sm100_params_size(void) { return static_cast<int64_t>(sizeof(Fa2FwdParams)); }
 
 const char* fa2_sm100_strerror(int status) {
@@ -673,6 +855,7 @@ const char* fa2_sm100_strerror(int status) {
     case FA2_ERR_LAUNCH: return "kernel launch failed";
     case FA2_ERR_DEVICE: return "current device is not sm_100 (B200) or the CUDA driver entry point is missing";
     case FA2_ERR_TIMEOUT: return "a bounded wait inside the kernel expired";
+    case FA2_ERR_WORKSPACE: return "num_splits > 1 needs a 16-byte aligned workspace of fa2_fwd_sm100_workspace_bytes() bytes";
     default: return "unknown fa2_sm100 status";
   }
 }
@@ -718,7 +901,19 @@ int fa2_fwd_sm100_check(const Fa2FwdParams* p) {
     return FA2_ERR_LAYOUT;
   }
   if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o)) return FA2_ERR_LAYOUT;
+  if (p->num_splits > 1) {
+    if (p->num_splits > 256) return FA2_ERR_SHAPE;
+    if (p->workspace == nullptr || !aligned16(p->workspace) ||
+        p->workspace_bytes < plan_splits(p).bytes) {
+      return FA2_ERR_WORKSPACE;
+    }
+  }
   return FA2_OK;
+}
+
+int64_t fa2_fwd_sm100_workspace_bytes(const Fa2FwdParams* p) {
+  if (p == nullptr) return 0;
+  return plan_splits(p).bytes;
 }
 
 int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream) {

@@ -10,7 +10,7 @@ import os
 LIB_NAME = "libfa2_sm100.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 FA2_DTYPE_FP16 = 0
 FA2_DTYPE_BF16 = 1
@@ -28,12 +28,14 @@ FA2_ERR_TMA_ENCODE = 9
 FA2_ERR_LAUNCH = 10
 FA2_ERR_DEVICE = 11
 FA2_ERR_TIMEOUT = 12
+FA2_ERR_WORKSPACE = 13
 
 # Every symbol the header declares (the ABI test checks the library exports all of them).
 EXPORTED = (
     "fa2_fwd_sm100_check",
     "fa2_fwd_sm100",
     "fa2_fwd_sm100_config",
+    "fa2_fwd_sm100_workspace_bytes",
     "fa2_sm100_strerror",
     "fa2_sm100_abi_version",
     "fa2_sm100_params_size",
@@ -65,6 +67,10 @@ class Fa2FwdParams(ctypes.Structure):
         ("err_flag", ctypes.c_void_p),
         ("timeout_cycles", ctypes.c_int64),
         ("gate", ctypes.c_void_p),
+        ("num_splits", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_int64),
     ]
 
 
@@ -101,6 +107,8 @@ def lib():
     L.fa2_sm100_strerror.restype = ctypes.c_char_p
     L.fa2_sm100_abi_version.argtypes = []
     L.fa2_sm100_abi_version.restype = ctypes.c_int
+    L.fa2_fwd_sm100_workspace_bytes.argtypes = [ctypes.POINTER(Fa2FwdParams)]
+    L.fa2_fwd_sm100_workspace_bytes.restype = ctypes.c_int64
     L.fa2_sm100_params_size.argtypes = []
     L.fa2_sm100_params_size.restype = ctypes.c_int64
     if L.fa2_sm100_abi_version() != ABI_VERSION:
@@ -129,7 +137,8 @@ def config(head_dim):
 
 def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stride,
                 batch, heads_q, heads_kv, seqlen_q, seqlen_kv, head_dim, dtype, causal,
-                pack_gqa, qk_scale, err_flag=0, timeout_cycles=0, gate=0):
+                pack_gqa, qk_scale, err_flag=0, timeout_cycles=0, gate=0, num_splits=1,
+                workspace=0, workspace_bytes=0):
     p = Fa2FwdParams()
     p.q, p.k, p.v, p.o = q_ptr, k_ptr, v_ptr, o_ptr
     p.q_stride[:] = list(q_stride)
@@ -143,7 +152,14 @@ def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stri
     p.err_flag = err_flag or None
     p.timeout_cycles = int(timeout_cycles)
     p.gate = gate or None
+    p.num_splits = int(num_splits)
+    p.workspace = workspace or None
+    p.workspace_bytes = int(workspace_bytes)
     return p
+
+
+def workspace_bytes(params):
+    return int(lib().fa2_fwd_sm100_workspace_bytes(ctypes.byref(params)))
 
 
 def check(params):

@@ -32,6 +32,9 @@ from . import _lib
 LOG2E = 1.4426950408889634
 KERNEL_BLOCK_M = 128
 KERNEL_BLOCK_N = 128
+CTA_ROWS = 256          # two 128-row Q tiles per CTA
+NUM_SMS_B200 = 148
+MAX_SPLITS = 16
 
 _err_words = {}
 
@@ -87,7 +90,24 @@ def _strides(t):
     return tuple(int(s) for s in t.stride())
 
 
-def _launch(q, k, v, out, causal, pack, qk_scale, timeout_cycles=0):
+def auto_num_splits(batch, heads_q, n_q, n_kv, group, pack, causal, num_sms=NUM_SMS_B200):
+    """Split-KV count for a launch (an extension; the reference has no split-KV). Splitting
+    pays when the (batch, head block, 256-row block) CTAs cannot fill the GPU and each has a
+    long K/V range, i.e. short queries against long K/V. One CTA fits per SM, so the split
+    CTAs are kept within one wave (measured: a second partial wave costs more than the split
+    gains), with at least 4 K/V tiles per split. Causal attention has N_q == N_kv and is not
+    split."""
+    if causal:
+        return 1
+    P = pack if pack else 1
+    ctas = batch * (heads_q // P) * (-(-(n_q * P) // CTA_ROWS))
+    tiles = -(-n_kv // KERNEL_BLOCK_N)
+    if 2 * ctas > num_sms or tiles < 8:
+        return 1
+    return max(1, min(MAX_SPLITS, num_sms // ctas, tiles // 4))
+
+
+def _launch(q, k, v, out, causal, pack, qk_scale, num_splits=1, timeout_cycles=0):
     B, H_q, N_q, D = q.shape
     H_kv, N_kv = k.shape[1], k.shape[2]
     err = _err_word(q.device)
@@ -96,23 +116,31 @@ def _launch(q, k, v, out, causal, pack, qk_scale, timeout_cycles=0):
         _strides(q), _strides(k), _strides(v), _strides(out),
         B, H_q, H_kv, N_q, N_kv, D,
         _lib.FA2_DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.FA2_DTYPE_FP16,
-        causal, pack, qk_scale, err.data_ptr(), timeout_cycles,
+        causal, pack, qk_scale, err.data_ptr(), timeout_cycles, num_splits=num_splits,
     )
+    ws = None
+    if num_splits > 1:
+        nbytes = _lib.workspace_bytes(p)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)  # caching allocator
+        p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    return _lib.launch(p, stream)
+    rc = _lib.launch(p, stream)
+    if ws is not None:
+        ws.record_stream(torch.cuda.current_stream(q.device))
+    return rc
 
 
-def _run(q, k, v, out, causal, pack, qk_scale):
+def _run(q, k, v, out, causal, pack, qk_scale, num_splits=1):
     with torch.cuda.device(q.device):
-        rc = _launch(q, k, v, out, causal, pack, qk_scale)
+        rc = _launch(q, k, v, out, causal, pack, qk_scale, num_splits)
         if rc == _lib.FA2_ERR_TMA_ENCODE and pack:
             pack = False  # bit-identical result; some stride orders only encode unpacked
-            rc = _launch(q, k, v, out, causal, pack, qk_scale)
+            rc = _launch(q, k, v, out, causal, pack, qk_scale, num_splits)
         if rc in (_lib.FA2_ERR_LAYOUT, _lib.FA2_ERR_TMA_ENCODE):
             # Layout copy (not a compute fallback): TMA needs 16-byte strides/alignment.
             qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
             oc = torch.empty_like(qc)
-            rc = _launch(qc, kc, vc, oc, causal, pack, qk_scale)
+            rc = _launch(qc, kc, vc, oc, causal, pack, qk_scale, num_splits)
             if rc == _lib.FA2_OK:
                 out.copy_(oc)
         if rc != _lib.FA2_OK:
@@ -121,12 +149,14 @@ def _run(q, k, v, out, causal, pack, qk_scale):
 
 
 def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
-              num_warps=None, num_stages=None, pack_gqa=None):
+              num_warps=None, num_stages=None, pack_gqa=None, num_splits=None):
     """softmax(Q K^T * sm_scale [+ causal mask]) V, fused (fa2/kernel.py:210-260).
 
     q: [B, H_q, N_q, D]; k, v: [B, H_kv, N_kv, D]; returns [B, H_q, N_q, D].
     pack_gqa: put each GQA group's query heads into one tile; None decides with
     should_pack_gqa. Asynchronous on torch's current stream, like the reference.
+    num_splits (extension, not in the reference): split-KV count; None picks one with
+    auto_num_splits (short queries against long K/V), 1 disables it.
     """
     assert q.dim() == k.dim() == v.dim() == 4
     B, H_q, N_q, D = q.shape
@@ -160,6 +190,10 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
     if not (q.device == k.device == v.device):
         raise RuntimeError("q, k and v must be on the same CUDA device")
 
+    if num_splits is None:
+        num_splits = auto_num_splits(B, H_q, N_q, N_kv, group, group if pack else 1, causal)
+    num_splits = max(1, int(num_splits))
+
     out = torch.empty_like(q)
     if out.numel() == 0:
         return out
@@ -167,7 +201,7 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
         pad = (0, 64 - D)
         qp, kp, vp = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
         op = torch.empty_like(qp)
-        _run(qp, kp, vp, op, causal, pack, qk_scale)
+        _run(qp, kp, vp, op, causal, pack, qk_scale, num_splits)
         out.copy_(op[..., :D])
         return out
-    return _run(q, k, v, out, causal, pack, qk_scale)
+    return _run(q, k, v, out, causal, pack, qk_scale, num_splits)
