@@ -48,8 +48,13 @@ enum Fa2Status {
   FA2_ERR_LAUNCH = 10,       /* the CUDA launch failed (cudaGetLastError) */
   FA2_ERR_DEVICE = 11,       /* current device is not sm_100 / driver entry point missing */
   FA2_ERR_TIMEOUT = 12,      /* value written to err_flag by a kernel whose bounded wait expired */
-  FA2_ERR_WORKSPACE = 13     /* num_splits > 1 without a large enough, 16-byte aligned workspace */
+  FA2_ERR_WORKSPACE = 13,    /* num_splits > 1 without a large enough, 16-byte aligned workspace */
+  FA2_ERR_SCRATCH_LIMIT = 14 /* fa2_fwd_sm100_noalloc: the split-KV scratch this call needs is
+                                larger than FA2_NOALLOC_SCRATCH_BYTES */
 };
+
+/* Size of the library-owned device scratch behind fa2_fwd_sm100_noalloc (32 MiB). */
+#define FA2_NOALLOC_SCRATCH_BYTES (32ll << 20)
 
 typedef struct Fa2FwdParams {
   const void* q;
@@ -100,6 +105,31 @@ FA2_API int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream);
 /* Bytes of device workspace fa2_fwd_sm100 needs for `p` (0 when p->num_splits <= 1).
  * Host only; the reference has no split-KV (its README lists it out of scope). */
 FA2_API int64_t fa2_fwd_sm100_workspace_bytes(const Fa2FwdParams* p);
+
+/* Split-KV forward that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory at call time: code running inside a
+ * CUDA graph being captured or a custom allocator callback, inference runtimes that own
+ * every device allocation and forbid cudaMalloc on the hot path, or plugins that receive
+ * only input and output pointers. Same contract as fa2_fwd_sm100, but the split-KV partials
+ * (fp32 partial O and row log-sum-exp, see fa2_fwd_sm100_workspace_bytes) go to a static
+ * device array of FA2_NOALLOC_SCRATCH_BYTES that belongs to this library; p->workspace and
+ * p->workspace_bytes are ignored. The caller still passes q, k, v and o.
+ *
+ * Limits and behaviour:
+ *  - returns FA2_ERR_SCRATCH_LIMIT (and launches nothing) when the call needs more scratch
+ *    than FA2_NOALLOC_SCRATCH_BYTES; use fewer splits or fa2_fwd_sm100 with a workspace;
+ *  - the array is created when the library's GPU code is loaded and every GPU that loads the
+ *    library holds it until the process exits;
+ *  - the first call on each device looks up the array's device address (once per device, with
+ *    that device current); make that first call before any stream capture;
+ *  - all calls share the one array and it keeps the previous call's contents (nothing in it
+ *    needs to start at zero: every slot a call reads is written earlier in the same call), so
+ *    calls that overlap on the GPU (other streams, other host threads) race on it: serialise
+ *    them, e.g. issue them on one stream;
+ *  - calls no cudaMalloc/cudaFree or allocating library routine.
+ * With num_splits <= 1 no scratch is used and this behaves as fa2_fwd_sm100. */
+FA2_API int fa2_fwd_sm100_noalloc(const Fa2FwdParams* p, void* stream);
 
 /* Static description of the compiled kernel family (fa2/kernel.py:186-195 analogue):
  * fills BLOCK_M, BLOCK_N, threads per CTA, K/V pipeline stages and dynamic shared memory

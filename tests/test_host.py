@@ -46,7 +46,7 @@ def test_config_entry_point():
 
 
 def test_strerror_covers_all_codes():
-    for code in range(0, 14):
+    for code in range(0, 15):
         assert _lib.strerror(code) != "unknown fa2_sm100 status"
     assert _lib.strerror(999) == "unknown fa2_sm100 status"
 

@@ -856,6 +856,7 @@ const char* fa2_sm100_strerror(int status) {
     case FA2_ERR_DEVICE: return "current device is not sm_100 (B200) or the CUDA driver entry point is missing";
     case FA2_ERR_TIMEOUT: return "a bounded wait inside the kernel expired";
     case FA2_ERR_WORKSPACE: return "num_splits > 1 needs a 16-byte aligned workspace of fa2_fwd_sm100_workspace_bytes() bytes";
+    case FA2_ERR_SCRATCH_LIMIT: return "fa2_fwd_sm100_noalloc: this call needs more split-KV scratch than the library's 32 MiB static array; use fewer splits or fa2_fwd_sm100 with a workspace";
     default: return "unknown fa2_sm100 status";
   }
 }
@@ -933,3 +934,37 @@ int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream) {
 }
 
 }  // extern "C"
+
+// ============================================================ allocation-free entry point
+// Split-KV scratch owned by the library, for callers that cannot allocate device memory
+// (see fa2_fwd_sm100_noalloc in fa2_sm100.h). In host code `g_noalloc_scratch` is only a
+// host-side stand-in for the symbol, never a device address: the address comes from
+// cudaGetSymbolAddress, looked up once per device below.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[FA2_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+void* g_noalloc_addr[kMaxDevices] = {};
+}  // namespace
+
+extern "C" int fa2_fwd_sm100_noalloc(const Fa2FwdParams* p, void* stream) {
+  if (p == nullptr) return FA2_ERR_NULL;
+  Fa2FwdParams q = *p;
+  q.workspace = nullptr;
+  q.workspace_bytes = 0;
+  if (q.num_splits > 1) {
+    if (plan_splits(&q).bytes > FA2_NOALLOC_SCRATCH_BYTES) return FA2_ERR_SCRATCH_LIMIT;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FA2_ERR_DEVICE;
+    if (g_noalloc_addr[dev] == nullptr) {
+      // Set-up, once per device, with that device current (done before any launch here).
+      void* addr = nullptr;
+      if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || addr == nullptr) {
+        return FA2_ERR_DEVICE;
+      }
+      g_noalloc_addr[dev] = addr;
+    }
+    q.workspace = g_noalloc_addr[dev];
+    q.workspace_bytes = FA2_NOALLOC_SCRATCH_BYTES;
+  }
+  return fa2_fwd_sm100(&q, stream);
+}

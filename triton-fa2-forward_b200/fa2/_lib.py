@@ -29,6 +29,8 @@ FA2_ERR_LAUNCH = 10
 FA2_ERR_DEVICE = 11
 FA2_ERR_TIMEOUT = 12
 FA2_ERR_WORKSPACE = 13
+FA2_ERR_SCRATCH_LIMIT = 14
+NOALLOC_SCRATCH_BYTES = 32 << 20
 
 # Every symbol the header declares (the ABI test checks the library exports all of them).
 EXPORTED = (
@@ -36,6 +38,7 @@ EXPORTED = (
     "fa2_fwd_sm100",
     "fa2_fwd_sm100_config",
     "fa2_fwd_sm100_workspace_bytes",
+    "fa2_fwd_sm100_noalloc",
     "fa2_sm100_strerror",
     "fa2_sm100_abi_version",
     "fa2_sm100_params_size",
@@ -107,6 +110,8 @@ def lib():
     L.fa2_sm100_strerror.restype = ctypes.c_char_p
     L.fa2_sm100_abi_version.argtypes = []
     L.fa2_sm100_abi_version.restype = ctypes.c_int
+    L.fa2_fwd_sm100_noalloc.argtypes = [ctypes.POINTER(Fa2FwdParams), ctypes.c_void_p]
+    L.fa2_fwd_sm100_noalloc.restype = ctypes.c_int
     L.fa2_fwd_sm100_workspace_bytes.argtypes = [ctypes.POINTER(Fa2FwdParams)]
     L.fa2_fwd_sm100_workspace_bytes.restype = ctypes.c_int64
     L.fa2_sm100_params_size.argtypes = []
