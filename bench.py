@@ -173,6 +173,43 @@ def cpu_baseline_sample(seconds=12.0, threads=None):
                       f"{el:.1f} s"}
 
 
+def triton_reference_same_box(q, k, v, steps=10, warmup=3):
+    """The reference's own Triton kernel (unmodified, installed in baseline/_ref) on the same
+    GPU and inputs, with the same protocol: TFLOP/s of its fa2.kernel.attention(causal=True).
+    Loaded under a private module name so it cannot shadow this repository's fa2 package.
+    Returns None when baseline/_ref is absent or the kernel fails here."""
+    import importlib.util
+
+    path = os.path.join(REPO, "baseline", "_ref", "fa2", "kernel.py")
+    if not os.path.exists(path):
+        return None
+    try:
+        spec = importlib.util.spec_from_file_location("reference_triton_fa2_kernel", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        fn = lambda: mod.attention(q, k, v, causal=True)  # noqa: E731
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=q.device)
+        ts = []
+        for _ in range(steps):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            ts.append(s.elapsed_time(e))
+        B, Hq, N, D = q.shape
+        ms = sum(ts) / len(ts)
+        return {"value": flops(B, Hq, N, D, True) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+                "what": "reference fa2.kernel.attention (Triton, unmodified, baseline/_ref) on this GPU, "
+                        "same inputs and protocol, rank 0's shard"}
+    except Exception as exc:  # reported, never fatal
+        return {"value": None, "error": f"{type(exc).__name__}: {exc}"[:200]}
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference's CPU path timed on the host cores (rank 0 only)."""
     if rank != 0:
@@ -324,6 +361,9 @@ def run_ours(args, world, rank, local):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(seconds=args.cpu_seconds)
+    triton_ref = None
+    if rank == 0 and world == 1 and not args.no_triton_ref:
+        triton_ref = triton_reference_same_box(q, k, v)
 
     if pg is not None:
         pg.barrier()
@@ -355,6 +395,8 @@ def run_ours(args, world, rank, local):
         line["replicated_out_allgather_ms"] = allgather_ms
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if triton_ref is not None:
+        line["reference_triton_same_gpu"] = triton_ref
     print(json.dumps(line), flush=True)
     return 0
 
@@ -368,6 +410,8 @@ def main():
     ap.add_argument("--replicate-out", action="store_true", help="also time the NCCL all-gather of O")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-triton-ref", action="store_true",
+                    help="skip timing the reference's Triton kernel from baseline/_ref")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         ap.error("--warmup must be >= 3")
