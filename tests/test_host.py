@@ -162,6 +162,7 @@ def test_auto_num_splits():
     from fa2.kernel import auto_num_splits
     assert auto_num_splits(2, 32, 8192, 8192, 4, 1, True) == 1          # causal prefill: never
     assert auto_num_splits(2, 32, 8192, 8192, 4, 1, False) == 1         # GPU already full
-    assert auto_num_splits(16, 32, 1, 4096, 4, 4, False) == 1           # 128 CTAs already ~ one wave
-    assert auto_num_splits(4, 32, 1, 65536, 4, 4, False) == 4           # 32 CTAs -> 128 in one wave
+    assert auto_num_splits(16, 32, 1, 4096, 4, 4, False) == 2           # decode: one split pair per CTA
+    assert auto_num_splits(4, 32, 1, 65536, 4, 4, False) == 8           # 32 CTAs -> 4 pairs each
+    assert auto_num_splits(2, 8, 200, 8192, 1, 1, False) == 9           # 200 rows (no pairs): 16 CTAs -> 144
     assert auto_num_splits(1, 8, 1, 512, 8, 8, False) == 1              # too few K/V tiles

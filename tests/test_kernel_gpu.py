@@ -326,3 +326,20 @@ def test_split_kv_noncontiguous_output_strides():
                for t in make_cuda_qkv(2, 8, 2, 9, 3000, 128, torch.float16))
     out = check_against_oracle(q, k, v, causal=False, num_splits=4)
     assert out.stride() == q.stride()
+
+
+@pytest.mark.parametrize("num_splits", [2, 3, 5, 8])
+@pytest.mark.parametrize("N_kv", [1000, 4096])
+def test_split_kv_dual_pairs(num_splits, N_kv):
+    """All query rows in one Q tile: the CTA's two Q-tile slots stream two splits of the same
+    rows. Odd counts round up to pairs, and a slot whose split lies past N_kv contributes
+    nothing."""
+    q, k, v = make_cuda_qkv(3, 16, 4, 7, N_kv, 128, torch.bfloat16)
+    out = check_against_oracle(q, k, v, causal=False, pack_gqa=True, num_splits=num_splits)
+    ref1 = attention(q, k, v, causal=False, pack_gqa=True, num_splits=1)
+    assert (out.float() - ref1.float()).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_split_kv_dual_fp16_unpacked(D):
+    check_against_oracle(*make_cuda_qkv(2, 4, 4, 100, 3000, D, torch.float16), causal=False, num_splits=4)

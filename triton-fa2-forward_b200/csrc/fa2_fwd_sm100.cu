@@ -119,6 +119,9 @@ struct KArgs {
   // split-KV: CTA (x, y, z) covers K/V tiles [z * split_tiles, (z + 1) * split_tiles) of its
   // range and writes fp32 O / l plus the row log2-sum-exp to the workspace (num_splits > 1).
   int num_splits, split_tiles, rows_pad;
+  // dual split (num_splits > 1, non-causal, all rows in Q tile 0): both Q-tile slots use the
+  // same 128 query rows, tile t walking split 2z + t, so a CTA streams two K/V ranges at once.
+  int dual;
   float* o_part;    // [num_splits][gridDim.x][rows_pad][D]
   float* lse_part;  // [num_splits][gridDim.x][rows_pad]
 };
@@ -225,11 +228,20 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   const int row0 = mb * (Q_TILES * BM);  // first packed row of this CTA
   static_assert(Q_TILES * BM == 256 && BN == 128, "cta_kv_tiles assumes 256-row CTAs, 128-row K/V tiles");
   const int J_cta = cta_kv_tiles<CAUSAL>(mb, a.n_q, a.n_kv, a.pack);  // K/V tiles of the CTA (>= 1)
-  int j0 = 0, J = J_cta;  // this CTA's share: tiles [j0, j0 + J)
+  int j0 = 0, J = J_cta;  // this CTA's share: tiles [j0, j0 + J) (tile 1 in dual mode: [j0b, j0b + J))
+  int j0b = 0;
+  const bool dual = (a.dual != 0);
   if (a.num_splits > 1) {
-    j0 = static_cast<int>(blockIdx.z) * a.split_tiles;
-    J = min(J_cta - j0, a.split_tiles);
-    if (J <= 0) return;  // split past this row block's band: nothing to do (uniform, before any sync)
+    if (dual) {
+      j0 = 2 * static_cast<int>(blockIdx.z) * a.split_tiles;
+      j0b = j0 + a.split_tiles;
+      J = a.split_tiles;  // tiles past N_kv load as zeros and are masked
+      if (j0 >= J_cta) return;
+    } else {
+      j0 = static_cast<int>(blockIdx.z) * a.split_tiles;
+      J = min(J_cta - j0, a.split_tiles);
+      if (J <= 0) return;  // split past this row block's band: nothing to do (uniform, before any sync)
+    }
   }
 
   if (warp == LOAD_WARP && lane == 0) {
@@ -291,22 +303,43 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         q0_issued = true;
       }
       int issued = 0;
-      for (int i = 0; ok && i < 2 * J; ++i) {
+      // Ring order == the MMA warp's consumption order. Normal: K0, V0, K1, V1, ... (each
+      // tile feeds both Q tiles). Dual: Ka0, Kb0, then per step j: Va_j, Ka_j+1, Vb_j, Kb_j+1.
+      const int n_tiles = dual ? 4 * J : 2 * J;
+      for (int i = 0; ok && i < n_tiles; ++i) {
         const int st = i % C::STAGES;
         const uint32_t ph = static_cast<uint32_t>(i / C::STAGES) & 1u;
         if (!mbar_wait(bar(C::B_KV_EMPTY + st), ph ^ 1u, a.timeout, a.err)) {
           ok = false;
           break;
         }
+        bool is_v;
+        int kv_tile;
+        if (!dual) {
+          is_v = (i & 1) != 0;
+          kv_tile = j0 + (i >> 1);
+        } else if (i < 2) {
+          is_v = false;
+          kv_tile = (i == 0) ? j0 : j0b;
+        } else {
+          const int g = (i - 2) >> 2, rr = (i - 2) & 3;
+          if (g == J - 1) {  // last step: Va, Vb
+            is_v = true;
+            kv_tile = (rr == 0 ? j0 : j0b) + g;
+          } else {
+            is_v = (rr & 1) == 0;
+            kv_tile = (rr < 2 ? j0 : j0b) + g + (is_v ? 0 : 1);
+          }
+        }
         mbar_arrive_expect_tx(bar(C::B_KV_FULL + st), C::TILE_BYTES);
-        const CUtensorMap* m = (i & 1) ? &tmV : &tmK;
+        const CUtensorMap* m = is_v ? &tmV : &tmK;
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c) {
           tma_load_4d(sbase + C::OFF_KV + st * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
-                      bar(C::B_KV_FULL + st), c * 64, (j0 + (i >> 1)) * BN, hkv, b, pol_kv);
+                      bar(C::B_KV_FULL + st), c * 64, kv_tile * BN, hkv, b, pol_kv);
         }
         ++issued;
-        if (i == 0) load_q(1);
+        if (i == 0 && !dual) load_q(1);
       }
       // Drain: every TMA write into this CTA's shared memory must land before the CTA
       // can exit, also when another role gave up early.
@@ -315,7 +348,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                   DEFAULT_TIMEOUT, nullptr);
       }
       if (q0_issued) mbar_wait(bar(C::B_Q + 0), 0, DEFAULT_TIMEOUT, nullptr);
-      if (issued > 0) mbar_wait(bar(C::B_Q + 1), 0, DEFAULT_TIMEOUT, nullptr);
+      if (issued > 0 && !dual) mbar_wait(bar(C::B_Q + 1), 0, DEFAULT_TIMEOUT, nullptr);
     }
   } else if (warp == MMA_WARP) {
     reg_dealloc<REGS_OTHER>();
@@ -329,7 +362,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       const uint64_t dk_base = sdesc_sw128(sbase + C::OFF_KV, 16, 1024);
       const uint64_t dv_base = sdesc_sw128(sbase + C::OFF_KV, C::CHUNK_BYTES, 1024);
       auto issue_qk = [&](int t, int st) {
-        const uint64_t qd = dq_base + static_cast<uint64_t>((t * C::TILE_BYTES) >> 4);
+        const int qt = dual ? 0 : t;  // dual: both tiles multiply Q tile 0
+        const uint64_t qd = dq_base + static_cast<uint64_t>((qt * C::TILE_BYTES) >> 4);
         const uint64_t kd = dk_base + static_cast<uint64_t>((st * C::TILE_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -363,41 +397,85 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       auto kv_wait = [&](int i) -> bool {
         return mwait(C::B_KV_FULL + i % C::STAGES, static_cast<uint32_t>(i / C::STAGES) & 1u);
       };
+      if (dual) {
+        // Each K/V tile feeds one Q tile; ci walks the ring in the loader's order.
+        int ci = 0;
+        auto take = [&]() -> int {
+          const int slot = ci++;
+          return kv_wait(slot) ? slot % C::STAGES : -1;
+        };
+        do {
+          if (!mwait(C::B_Q + 0, 0)) { ok = false; break; }
+          int sa = take();
+          if (sa < 0) { ok = false; break; }
+          tc_fence_after();
+          issue_qk(0, sa);
+          mma_commit(bar(C::B_S_FULL + 0));
+          mma_commit(bar(C::B_KV_EMPTY + sa));
+          int sb = take();
+          if (sb < 0) { ok = false; break; }
+          tc_fence_after();
+          issue_qk(1, sb);
+          mma_commit(bar(C::B_S_FULL + 1));
+          mma_commit(bar(C::B_KV_EMPTY + sb));
+          for (int j = 0; j < J; ++j) {
+            const bool more = (j + 1 < J);
+            const uint32_t pph = static_cast<uint32_t>(j) & 1u;
+            for (int t = 0; t < 2; ++t) {
+              const int sv = take();
+              if (sv < 0 || !pv_tile(t, sv, j > 0, pph)) { ok = false; break; }
+              mma_commit(bar(C::B_KV_EMPTY + sv));
+              if (more) {
+                const int sk = take();
+                if (sk < 0) { ok = false; break; }
+                tc_fence_after();
+                issue_qk(t, sk);
+                mma_commit(bar(C::B_S_FULL + t));
+                mma_commit(bar(C::B_KV_EMPTY + sk));
+              } else {
+                mma_commit(bar(C::B_O_FULL + t));
+              }
+            }
+            if (!ok) break;
+          }
+        } while (false);
+      } else {
       do {
-        if (!mwait(C::B_Q + 0, 0) || !kv_wait(0)) { ok = false; break; }
-        tc_fence_after();
-        issue_qk(0, 0);
-        mma_commit(bar(C::B_S_FULL + 0));
-        if (!mwait(C::B_Q + 1, 0)) { ok = false; break; }
-        tc_fence_after();
-        issue_qk(1, 0);
-        mma_commit(bar(C::B_S_FULL + 1));
-        mma_commit(bar(C::B_KV_EMPTY + 0));
-        for (int j = 0; j < J; ++j) {
-          const int iv = 2 * j + 1, ik = 2 * j + 2;
-          const int sv = iv % C::STAGES, sk = ik % C::STAGES;
-          const bool more = (j + 1 < J);
-          const uint32_t pph = static_cast<uint32_t>(j) & 1u;
-          if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
-          if (more) {
-            if (!kv_wait(ik)) { ok = false; break; }
-            tc_fence_after();
-            issue_qk(0, sk);
-            mma_commit(bar(C::B_S_FULL + 0));
-          } else {
-            mma_commit(bar(C::B_O_FULL + 0));
+          if (!mwait(C::B_Q + 0, 0) || !kv_wait(0)) { ok = false; break; }
+          tc_fence_after();
+          issue_qk(0, 0);
+          mma_commit(bar(C::B_S_FULL + 0));
+          if (!mwait(C::B_Q + 1, 0)) { ok = false; break; }
+          tc_fence_after();
+          issue_qk(1, 0);
+          mma_commit(bar(C::B_S_FULL + 1));
+          mma_commit(bar(C::B_KV_EMPTY + 0));
+          for (int j = 0; j < J; ++j) {
+            const int iv = 2 * j + 1, ik = 2 * j + 2;
+            const int sv = iv % C::STAGES, sk = ik % C::STAGES;
+            const bool more = (j + 1 < J);
+            const uint32_t pph = static_cast<uint32_t>(j) & 1u;
+            if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
+            if (more) {
+              if (!kv_wait(ik)) { ok = false; break; }
+              tc_fence_after();
+              issue_qk(0, sk);
+              mma_commit(bar(C::B_S_FULL + 0));
+            } else {
+              mma_commit(bar(C::B_O_FULL + 0));
+            }
+            if (!pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
+            mma_commit(bar(C::B_KV_EMPTY + sv));
+            if (more) {
+              issue_qk(1, sk);
+              mma_commit(bar(C::B_S_FULL + 1));
+              mma_commit(bar(C::B_KV_EMPTY + sk));
+            } else {
+              mma_commit(bar(C::B_O_FULL + 1));
+            }
           }
-          if (!pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
-          mma_commit(bar(C::B_KV_EMPTY + sv));
-          if (more) {
-            issue_qk(1, sk);
-            mma_commit(bar(C::B_S_FULL + 1));
-            mma_commit(bar(C::B_KV_EMPTY + sk));
-          } else {
-            mma_commit(bar(C::B_O_FULL + 1));
-          }
-        }
-      } while (false);
+        } while (false);
+      }
       // Every issued MMA must retire before TMEM is released.
       mma_commit(bar(C::B_MMA_DONE));
       mbar_wait(bar(C::B_MMA_DONE), 0, DEFAULT_TIMEOUT, nullptr);
@@ -412,7 +490,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t tS = tmem + lane_addr + t * BN;
     const uint32_t tP = tS + BN / 2;
     const uint32_t tO = tmem + lane_addr + C::TMEM_O + t * D;
-    const int tile_row0 = row0 + t * BM;
+    const int tile_row0 = row0 + (dual ? 0 : t * BM);  // dual: both tiles hold Q tile 0's rows
+    const int kv_base = (dual && t == 1) ? j0b : j0;   // first K/V tile of this tile's range
     const int pos = (tile_row0 + r) / a.pack;    // sequence position of this row
     const int tile_pos0 = tile_row0 / a.pack;    // position of the tile's first row
     const float qk_scale = a.qk_scale;
@@ -424,7 +503,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(j) & 1u, a.timeout, a.err);
       if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       tc_fence_after();
-      const int col0 = (j0 + j) * BN;
+      const int col0 = (kv_base + j) * BN;
       const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
       const bool need_pad = (col0 + BN > a.n_kv);
       const bool masked = need_causal || need_pad;  // uniform over the warpgroup
@@ -538,7 +617,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       tc_fence_after();
       const bool has = (l > 0.0f);
       const float inv_l = has ? 1.0f / l : 0.0f;
-      const int64_t slot = (static_cast<int64_t>(blockIdx.z) * gridDim.x + blockIdx.x) * a.rows_pad + tile_row0 + r;
+      const int split_idx = dual ? 2 * static_cast<int>(blockIdx.z) + t : static_cast<int>(blockIdx.z);
+      const int64_t slot = (static_cast<int64_t>(split_idx) * gridDim.x + blockIdx.x) * a.rows_pad + tile_row0 + r;
       float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D);
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -707,7 +787,7 @@ bool make_map(CUtensorMap* m, bool bf16, const void* base, const int64_t dims[4]
 constexpr int kMaxDevices = 64;
 
 struct SplitPlan {
-  int num_splits = 1, split_tiles = 0, rows_pad = 0, xblocks = 0;
+  int num_splits = 1, split_tiles = 0, rows_pad = 0, xblocks = 0, dual = 0, grid_z = 1;
   int64_t bytes = 0;
 };
 
@@ -719,8 +799,12 @@ SplitPlan plan_splits(const Fa2FwdParams* p) {
   const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
   const int mblocks = static_cast<int>((rows + 255) / 256);
   const int j_max = (p->seqlen_kv + 127) / 128;
-  sp.num_splits = p->num_splits;
-  sp.split_tiles = (j_max + p->num_splits - 1) / p->num_splits;
+  // Dual mode: every query row sits in the CTA's first Q tile (short queries, no causal
+  // band), so the second tile slot walks another split of the same rows; splits come in pairs.
+  sp.dual = (!p->causal && rows <= 128) ? 1 : 0;
+  sp.num_splits = sp.dual ? ((p->num_splits + 1) / 2) * 2 : p->num_splits;
+  sp.grid_z = sp.dual ? sp.num_splits / 2 : sp.num_splits;
+  sp.split_tiles = (j_max + sp.num_splits - 1) / sp.num_splits;
   sp.rows_pad = mblocks * 256;
   sp.xblocks = p->batch * (p->heads_q / pack);
   sp.bytes = static_cast<int64_t>(sp.num_splits) * sp.xblocks * sp.rows_pad * (p->head_dim + 1) * 4 + 256;
@@ -777,6 +861,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.num_splits = sp.num_splits;
   ka.split_tiles = sp.split_tiles;
   ka.rows_pad = sp.rows_pad;
+  ka.dual = sp.dual;
   ka.o_part = nullptr;
   ka.lse_part = nullptr;
   if (sp.num_splits > 1) {
@@ -789,7 +874,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
   const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(p->batch) * ka.hblocks),
                   static_cast<unsigned>((rows + fa2::Q_TILES * fa2::BM - 1) / (fa2::Q_TILES * fa2::BM)),
-                  static_cast<unsigned>(sp.num_splits));
+                  static_cast<unsigned>(sp.grid_z));
   kern<<<grid, fa2::NUM_THREADS, C::SMEM_ALLOC, stream>>>(tmQ, tmK, tmV, tmO, ka);
   if (cudaGetLastError() != cudaSuccess) return FA2_ERR_LAUNCH;
   if (sp.num_splits > 1) {

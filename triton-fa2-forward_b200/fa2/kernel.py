@@ -102,7 +102,14 @@ def auto_num_splits(batch, heads_q, n_q, n_kv, group, pack, causal, num_sms=NUM_
     P = pack if pack else 1
     ctas = batch * (heads_q // P) * (-(-(n_q * P) // CTA_ROWS))
     tiles = -(-n_kv // KERNEL_BLOCK_N)
-    if 2 * ctas > num_sms or tiles < 8:
+    if tiles < 8:
+        return 1
+    if n_q * P <= KERNEL_BLOCK_M:
+        # All rows fit the first Q tile: splits run in pairs inside one CTA (the second Q-tile
+        # slot streams the other split of the same rows), so 2 splits add no CTAs.
+        z = max(1, min(MAX_SPLITS // 2, num_sms // ctas, tiles // 8))
+        return 2 * z
+    if 2 * ctas > num_sms:
         return 1
     return max(1, min(MAX_SPLITS, num_sms // ctas, tiles // 4))
 
