@@ -210,6 +210,44 @@ def triton_reference_same_box(q, k, v, steps=10, warmup=3):
         return {"value": None, "error": f"{type(exc).__name__}: {exc}"[:200]}
 
 
+def decode_secondary(dev, steps=10):
+    """Secondary workload (not the headline metric): one new query token per sequence against a
+    long K/V, the reference's short-query case (GQA-packed, here split-KV in pairs). Bound by
+    HBM: algorithmic bytes = K + V + Q + O; reported as GB/s against the measured copy peak."""
+    from fa2.kernel import attention
+
+    B, Hq, Hkv, Nkv, D = 4, 32, 8, 65536, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    q = torch.randn(B, Hq, 1, D, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(B, Hkv, Nkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(B, Hkv, Nkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+    fn = lambda: attention(q, k, v, causal=False)  # noqa: E731
+    for _ in range(3):
+        fn()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ts = []
+    for _ in range(steps):
+        flush.fill_(1)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize(dev)
+        ts.append(s.elapsed_time(e))
+    ms = sum(ts) / len(ts)
+    nbytes = 2 * k.numel() * 2 + 2 * q.numel() * 2
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["hbm_gbs"])
+    except Exception:
+        peak = 6650.0
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": f"decode: B={B} Hq={Hq} Hkv={Hkv} N_q=1 N_kv={Nkv} D={D} bf16 non-causal",
+            "ms": ms, "GB/s": gbs, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak,
+                                                "unit": "GB/s", "frac": gbs / peak},
+            "launches_per_step": 2}
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference's CPU path timed on the host cores (rank 0 only)."""
     if rank != 0:
@@ -391,6 +429,9 @@ def run_ours(args, world, rank, local):
     triton_ref = None
     if rank == 0 and world == 1 and not args.no_triton_ref:
         triton_ref = triton_reference_same_box(q, k, v)
+    decode = None
+    if rank == 0 and world == 1 and not args.no_secondary:
+        decode = decode_secondary(dev)
 
     if pg is not None:
         pg.barrier()
@@ -426,6 +467,8 @@ def run_ours(args, world, rank, local):
         line["cpu_baseline"] = cpu
     if triton_ref is not None:
         line["reference_triton_same_gpu"] = triton_ref
+    if decode is not None:
+        line["secondary_decode"] = decode
     print(json.dumps(line), flush=True)
     return 0
 
@@ -439,6 +482,7 @@ def main():
     ap.add_argument("--replicate-out", action="store_true", help="also time the NCCL all-gather of O")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-secondary", action="store_true", help="skip the secondary decode workload")
     ap.add_argument("--no-triton-ref", action="store_true",
                     help="skip timing the reference's Triton kernel from baseline/_ref")
     args = ap.parse_args()

@@ -24,6 +24,8 @@ CONFIGS = {
     "headline": (2, 32, 8, 8192, 128, torch.bfloat16, True, 1.0),
     "full_long": (2, 32, 32, 16384, 64, torch.float16, False, 0.5),
     "pack_tail": (16, 64, 8, 1000, 128, torch.bfloat16, True, 1.0),
+    # short query against a long K/V (decode): HBM-bound, GQA-packed, split-KV in pairs
+    "decode": (4, 32, 8, (1, 65536), 128, torch.bfloat16, False, 1.0),
 }
 
 
@@ -35,10 +37,11 @@ def main():
     ap.add_argument("--pack", choices=["auto", "on", "off"], default="auto")
     args = ap.parse_args()
     B, Hq, Hkv, N, D, dt, causal, scale = CONFIGS[args.config]
+    n_q, n_kv = N if isinstance(N, tuple) else (N, N)
     g = torch.Generator(device="cuda").manual_seed(0)
-    q = torch.randn(B, Hq, N, D, device="cuda", dtype=dt, generator=g) * scale
-    k = torch.randn(B, Hkv, N, D, device="cuda", dtype=dt, generator=g) * scale
-    v = torch.randn(B, Hkv, N, D, device="cuda", dtype=dt, generator=g) * scale
+    q = torch.randn(B, Hq, n_q, D, device="cuda", dtype=dt, generator=g) * scale
+    k = torch.randn(B, Hkv, n_kv, D, device="cuda", dtype=dt, generator=g) * scale
+    v = torch.randn(B, Hkv, n_kv, D, device="cuda", dtype=dt, generator=g) * scale
     pack = {"auto": None, "on": True, "off": False}[args.pack]
     for _ in range(args.warmup + args.launches):
         attention(q, k, v, causal=causal, pack_gqa=pack)
