@@ -80,6 +80,24 @@ def test_kernel_noncausal_different_lengths():
     check_against_oracle(*make_cuda_qkv(2, 4, 2, 23, 70, 64, torch.float16), causal=False)
 
 
+# ------------------------------------------------------- persistent unit walk
+# One CTA per SM walks the work units (a 256-row block of one (batch, head block)). These
+# shapes give every CTA several units of one K/V tile each, unit counts just above one and
+# exactly two waves of 148, and causal units of every length on the same CTA.
+@pytest.mark.parametrize("B,H,H_kv,N,causal,D,dtype", [
+    (8, 40, 40, 96, False, 64, torch.float16),      # 320 units, J = 1 each
+    (8, 40, 40, 96, True, 128, torch.bfloat16),
+    (1, 149, 149, 256, True, 128, torch.bfloat16),  # 149 units: one CTA takes two
+    (1, 149, 149, 300, False, 64, torch.float16),   # 298 units, ragged last block
+    (2, 37, 37, 1000, True, 128, torch.float16),    # 296 units = 2 x 148
+    (3, 99, 99, 513, True, 64, torch.bfloat16),     # 891 units, J from 1 to 5
+    (3, 45, 9, 700, True, 128, torch.bfloat16),     # GQA group 5 (unpacked), 405 units
+    (5, 21, 7, 333, False, 128, torch.float16),     # GQA group 3, 210 units
+])
+def test_persistent_unit_walk(B, H, H_kv, N, causal, D, dtype):
+    check_against_oracle(*make_cuda_qkv(B, H, H_kv, N, N, D, dtype, seed=B + H), causal)
+
+
 @pytest.mark.parametrize("N_q,N_kv", [(1, 1), (1, 300), (5, 129), (129, 5), (300, 128)])
 def test_kernel_noncausal_ragged(N_q, N_kv):
     check_against_oracle(*make_cuda_qkv(2, 8, 2, N_q, N_kv, 128, torch.bfloat16), causal=False)

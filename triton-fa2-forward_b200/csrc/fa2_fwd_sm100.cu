@@ -5,11 +5,16 @@
 //   fa2/kernel.py:60-107   _attn_fwd_inner  (per K/V tile: S = QK^T, mask, online softmax, PV)
 //   fa2/kernel.py:210-260  attention()      (validation, pack decision, launch)
 //
-// One CTA owns two Q tiles of 128 rows (256 rows; with GQA packing a row is a
+// A work unit is two Q tiles of 128 rows (256 rows; with GQA packing a row is a
 // (position, head) pair, row r -> position r / PACK, head r % PACK, fa2/kernel.py:135-141)
-// of one (batch, q-head block) and walks the K/V tiles [0, J) it can see, in increasing
+// of one (batch, q-head block); it walks the K/V tiles [0, J) it can see, in increasing
 // order (the reference's order: stage 1 unmasked tiles from column 0, then the diagonal
 // band, nothing to its right; fa2/kernel.py:150-175).
+// The launch is persistent: one CTA per SM walks a static list of units (heaviest causal
+// row blocks first, snake order over the CTAs). The K/V ring, the TMEM accumulators and the
+// barrier phases carry over from one unit to the next, so the next unit's Q and K_0 load
+// and its first QK GEMMs run while the softmax warps finish and store the previous unit.
+// (With split-KV the grid has one CTA per (unit, split) instead.)
 //
 // Warp roles (384 threads, three warpgroups):
 //   warps 0-3   softmax for Q tile 0   (thread = one row = one TMEM lane; warp w reaches
@@ -19,7 +24,7 @@
 //   warp  9     TMA producer (one thread)
 //   warps 10-11 idle
 // Registers: launched at 168/thread; setmaxnreg moves them to the softmax warpgroups
-// (208 each) from the MMA/TMA warpgroup (88): 2 * 208 + 88 == 3 * 168.
+// (200 each) from the MMA/TMA warpgroup (104): 2 * 200 + 104 == 3 * 168.
 // TMEM (512 columns x 128 lanes, fp32):  S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [..+D)
 //   P_t (fp16/bf16, packed 2 per column) overwrites the upper half of S_t, and the second
 //   GEMM reads it straight from TMEM (tcgen05.mma A-from-TMEM).
@@ -58,8 +63,8 @@ constexpr int SOFTMAX_WARPS = 8;
 constexpr int MMA_WARP = 8;
 constexpr int LOAD_WARP = 9;
 constexpr int TMEM_COLS = 512;
-constexpr int REGS_SOFTMAX = 208;
-constexpr int REGS_OTHER = 88;
+constexpr int REGS_SOFTMAX = 200;
+constexpr int REGS_OTHER = 104;
 constexpr float RESCALE_TH = 8.0f;               // log2 units: P may reach 2^8 before a rescale
 constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_EMU_MASK
@@ -71,15 +76,14 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_MMA_SPIN
 #define FA2_MMA_SPIN 0  // 1: the MMA thread polls its barriers without suspending (measured: no gain)
 #endif
-#ifndef FA2_P_ALL_FIRST
-#define FA2_P_ALL_FIRST 0  // 1: compute all of P before the first TMEM store (else store per chunk)
-#endif
-#ifndef FA2_SEQ_SOFTMAX
-#define FA2_SEQ_SOFTMAX 0  // 1: the two tiles' exp phases take turns instead of overlapping
+#ifndef FA2_PERSISTENT
+#define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
 #endif
 constexpr uint32_t EMU_PAIR_MASK = FA2_EMU_MASK;
 constexpr int P_SPLIT = FA2_P_SPLIT;
 static_assert(P_SPLIT >= 1 && P_SPLIT <= 3, "P hand-off split");
+// setmaxnreg draws on the registers the CTA was launched with (384 threads x 168).
+static_assert(2 * REGS_SOFTMAX + REGS_OTHER <= 3 * 168, "register split exceeds the launch budget");
 
 template <int D>
 struct Cfg {
@@ -90,7 +94,11 @@ struct Cfg {
   static constexpr int STAGES = (D == 128) ? 4 : 8; // K/V ring depth (K_j and V_j take one slot each)
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = Q_TILES * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_KV + STAGES * TILE_BYTES;
+  // O staging for the TMA store: one slot of 32 rows x 64 columns (128-byte swizzle, the
+  // O tensor map's box) per softmax warp.
+  static constexpr int STG_SLOT_BYTES = 32 * 128;
+  static constexpr int OFF_STG = OFF_KV + STAGES * TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + SOFTMAX_WARPS * STG_SLOT_BYTES;
   // barrier slots
   static constexpr int B_Q = 0;                     // [2]  Q tile landed
   static constexpr int B_KV_FULL = 2;               // [S]  K/V tile landed
@@ -100,7 +108,7 @@ struct Cfg {
   static constexpr int B_O_FULL = 6 + 2 * STAGES;   // [2]  last PV of tile t retired
   static constexpr int B_MMA_DONE = 8 + 2 * STAGES; // [1]  every MMA retired (teardown)
   static constexpr int B_P_LATE = 9 + 2 * STAGES;   // [2]  the remaining P_t columns in TMEM
-  static constexpr int B_SEQ = 11 + 2 * STAGES;     // [2]  exp phase of tile t done (turn-taking)
+  static constexpr int B_Q_EMPTY = 11 + 2 * STAGES; // [2]  last QK of tile t of a unit retired: Q_t reloadable
   static constexpr int NUM_BARS = 13 + 2 * STAGES;
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
@@ -110,12 +118,47 @@ struct Cfg {
   static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
 };
 
+// Division of 0 <= n < 2^31 by a divisor d >= 1 fixed at launch, as a multiply-high, an add
+// and a shift (Granlund & Montgomery, "Division by invariant integers using multiplication",
+// PLDI 1994): with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// n / d == (umulhi(n, m) + n) >> l. Unit decoding runs between a unit's last softmax step
+// and the next unit's first one, where a hardware-free division chain is on the critical path.
+struct FastDiv {
+  uint32_t d, m, l;
+  __host__ __device__ __forceinline__ uint32_t div(uint32_t n) const { return (__umulhi_hd(n, m) + n) >> l; }
+  __host__ __device__ __forceinline__ static uint32_t __umulhi_hd(uint32_t a, uint32_t b) {
+#ifdef __CUDA_ARCH__
+    return __umulhi(a, b);
+#else
+    return static_cast<uint32_t>((static_cast<uint64_t>(a) * b) >> 32);
+#endif
+  }
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  FastDiv f;
+  f.d = d;
+  f.l = 0;
+  while ((1ull << f.l) < d) ++f.l;
+  f.m = static_cast<uint32_t>(((1ull << 32) * ((1ull << f.l) - d)) / d + 1ull);
+  return f;
+}
+
 struct KArgs {
   int n_q, n_kv, group, pack, hblocks;  // hblocks = H_q / pack
+  int pack_shift;                       // pack == 1 << pack_shift (pack divides 128)
+  FastDiv div_xblocks, div_hblocks, div_group;
   float qk_scale;
   int* err;
   const int* gate;
   long long timeout;
+  // Work units: (256-row block mb, batch x head block x), xblocks * mblocks of them.
+  // persistent != 0 (no split-KV): gridDim.x CTAs, one per SM, walk the units in the order
+  // u = mi * xblocks + x with mi = 0 the heaviest causal block; CTA c takes u = n * G + c in
+  // even rounds n and u = n * G + (G - 1 - c) in odd ones (a snake, so each CTA gets a similar
+  // mix of long and short causal blocks). Otherwise the grid is (xblocks, mblocks, splits) and
+  // each CTA does the one unit of its block index.
+  int persistent, xblocks, mblocks, num_units;
   // split-KV: CTA (x, y, z) covers K/V tiles [z * split_tiles, (z + 1) * split_tiles) of its
   // range and writes fp32 O / l plus the row log2-sum-exp to the workspace (num_splits > 1).
   int num_splits, split_tiles, rows_pad;
@@ -127,14 +170,62 @@ struct KArgs {
 };
 
 // K/V tiles a CTA of 256-row block mb visits (>= 1): its causal band end, or all of N_kv.
+// pack == 1 << pack_shift.
 template <bool CAUSAL>
-__host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, int pack) {
+__host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, int pack_shift) {
   int kv_end = n_kv;
   if (CAUSAL) {
-    const int last_pos = min((mb * 256 + 255) / pack, n_q - 1);
+    const int last_pos = min((mb * 256 + 255) >> pack_shift, n_q - 1);
     kv_end = min(last_pos + 1, n_kv);
   }
   return (kv_end + 127) / 128;
+}
+
+// One work unit: packed Q rows [row0, row0 + 256) of batch b, q heads from hq0 (K/V head hkv),
+// against K/V tiles [j0, j0 + J) (in dual mode the second Q-tile slot walks [j0b, j0b + J)).
+struct Unit {
+  int x, b, hq0, hkv, row0, j0, j0b, J;
+};
+
+// Unit n of this CTA; false when the CTA has no n-th unit. J == 0: the unit is empty (a split
+// past its row block's causal band).
+template <bool CAUSAL>
+__device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
+  int mb, z = 0;
+  if (a.persistent) {
+    // n * G + c < num_units + G < 2^32: 32-bit unsigned arithmetic is exact.
+    const uint32_t G = gridDim.x, c = blockIdx.x, nn = static_cast<uint32_t>(n);
+    const uint32_t idx = nn * G + ((nn & 1u) ? (G - 1u - c) : c);
+    if (idx >= static_cast<uint32_t>(a.num_units)) return false;
+    const uint32_t mi = a.div_xblocks.div(idx);
+    u.x = static_cast<int>(idx - mi * a.div_xblocks.d);
+    mb = CAUSAL ? a.mblocks - 1 - static_cast<int>(mi) : static_cast<int>(mi);
+  } else {
+    if (n > 0) return false;
+    u.x = static_cast<int>(blockIdx.x);
+    mb = CAUSAL ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : static_cast<int>(blockIdx.y);
+    z = static_cast<int>(blockIdx.z);
+  }
+  u.b = static_cast<int>(a.div_hblocks.div(static_cast<uint32_t>(u.x)));
+  u.hq0 = (u.x - u.b * a.hblocks) << a.pack_shift;
+  u.hkv = static_cast<int>(a.div_group.div(static_cast<uint32_t>(u.hq0)));
+  static_assert(Q_TILES * BM == 256 && BN == 128, "cta_kv_tiles assumes 256-row CTAs, 128-row K/V tiles");
+  u.row0 = mb * (Q_TILES * BM);
+  const int J_cta = cta_kv_tiles<CAUSAL>(mb, a.n_q, a.n_kv, a.pack_shift);
+  u.j0 = 0;
+  u.j0b = 0;
+  u.J = J_cta;
+  if (a.num_splits > 1) {
+    if (a.dual) {
+      u.j0 = 2 * z * a.split_tiles;
+      u.j0b = u.j0 + a.split_tiles;
+      u.J = (u.j0 < J_cta) ? a.split_tiles : 0;  // tiles past N_kv load as zeros and are masked
+    } else {
+      u.j0 = z * a.split_tiles;
+      u.J = max(0, min(J_cta - u.j0, a.split_tiles));
+    }
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------- softmax helpers
@@ -219,44 +310,25 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // Work unit: (batch b, q-head block hb) on x, 256-row block on y (heaviest causal first).
-  const int b = blockIdx.x / a.hblocks;
-  const int hq0 = (blockIdx.x % a.hblocks) * a.pack;
-  const int hkv = hq0 / a.group;
-  const int mb = CAUSAL ? static_cast<int>(gridDim.y - 1 - blockIdx.y) : static_cast<int>(blockIdx.y);
-  const int row0 = mb * (Q_TILES * BM);  // first packed row of this CTA
-  static_assert(Q_TILES * BM == 256 && BN == 128, "cta_kv_tiles assumes 256-row CTAs, 128-row K/V tiles");
-  const int J_cta = cta_kv_tiles<CAUSAL>(mb, a.n_q, a.n_kv, a.pack);  // K/V tiles of the CTA (>= 1)
-  int j0 = 0, J = J_cta;  // this CTA's share: tiles [j0, j0 + J) (tile 1 in dual mode: [j0b, j0b + J))
-  int j0b = 0;
+  // Dual mode exists only with split-KV, which is never persistent: one unit per CTA.
   const bool dual = (a.dual != 0);
-  if (a.num_splits > 1) {
-    if (dual) {
-      j0 = 2 * static_cast<int>(blockIdx.z) * a.split_tiles;
-      j0b = j0 + a.split_tiles;
-      J = a.split_tiles;  // tiles past N_kv load as zeros and are masked
-      if (j0 >= J_cta) return;
-    } else {
-      j0 = static_cast<int>(blockIdx.z) * a.split_tiles;
-      J = min(J_cta - j0, a.split_tiles);
-      if (J <= 0) return;  // split past this row block's band: nothing to do (uniform, before any sync)
-    }
+  {
+    Unit u0;
+    if (!get_unit<CAUSAL>(a, 0, u0) || u0.J <= 0) return;  // nothing to do (uniform, before any sync)
   }
 
   if (warp == LOAD_WARP && lane == 0) {
-    mbar_init(bar(C::B_Q + 0), 1);
-    mbar_init(bar(C::B_Q + 1), 1);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(bar(C::B_KV_FULL + s), 1);
-      mbar_init(bar(C::B_KV_EMPTY + s), 1);
-    }
     for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(C::B_Q + t), 1);
+      mbar_init(bar(C::B_Q_EMPTY + t), 1);
       mbar_init(bar(C::B_S_FULL + t), 1);
       mbar_init(bar(C::B_P_FULL + t), BM);
       mbar_init(bar(C::B_P_LATE + t), BM);
-      mbar_init(bar(C::B_SEQ + t), BM);
       mbar_init(bar(C::B_O_FULL + t), 1);
+    }
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar(C::B_KV_FULL + s), 1);
+      mbar_init(bar(C::B_KV_EMPTY + s), 1);
     }
     mbar_init(bar(C::B_MMA_DONE), 1);
     fence_mbar_init();
@@ -284,71 +356,87 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       tma_prefetch_desc(&tmO);
       const uint64_t pol_kv = l2_policy_evict_last();   // K/V are re-read by every Q block
       const uint64_t pol_q = l2_policy_evict_first();   // Q is read once
-      auto load_q = [&](int t) {
-        const int R = row0 + t * BM;
-        const int pos = R / a.pack;
-        const int h = hq0 + R % a.pack;
+      int q_loads0 = 0, q_loads1 = 0;
+      auto load_q = [&](const Unit& u, int t) {
+        const int R = u.row0 + t * BM;
+        const int pos = R >> a.pack_shift;
+        const int h = u.hq0 + (R & (a.pack - 1));
         mbar_arrive_expect_tx(bar(C::B_Q + t), C::TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c) {
           tma_load_4d(sbase + C::OFF_Q + t * C::TILE_BYTES + c * C::CHUNK_BYTES, &tmQ, bar(C::B_Q + t),
-                      c * 64, h, pos, b, pol_q);
+                      c * 64, h, pos, u.b, pol_q);
         }
+        if (t == 0) ++q_loads0; else ++q_loads1;
       };
       // Optional start gate: no load is issued before *gate != 0 (bounded like every wait).
-      bool q0_issued = false;
       if (a.gate != nullptr) ok = flag_wait(a.gate, a.timeout, a.err);
-      if (ok) {
-        load_q(0);
-        q0_issued = true;
-      }
-      int issued = 0;
-      // Ring order == the MMA warp's consumption order. Normal: K0, V0, K1, V1, ... (each
-      // tile feeds both Q tiles). Dual: Ka0, Kb0, then per step j: Va_j, Ka_j+1, Vb_j, Kb_j+1.
-      const int n_tiles = dual ? 4 * J : 2 * J;
-      for (int i = 0; ok && i < n_tiles; ++i) {
-        const int st = i % C::STAGES;
-        const uint32_t ph = static_cast<uint32_t>(i / C::STAGES) & 1u;
-        if (!mbar_wait(bar(C::B_KV_EMPTY + st), ph ^ 1u, a.timeout, a.err)) {
+      int i = 0;  // K/V tiles issued into the ring, over all units
+      for (int n = 0; ok; ++n) {
+        Unit u;
+        if (!get_unit<CAUSAL>(a, n, u)) break;
+        // Q_t's buffer is free once the last QK GEMM of tile t of the previous unit retired.
+        if (n > 0 && !mbar_wait(bar(C::B_Q_EMPTY + 0), static_cast<uint32_t>(n - 1) & 1u, a.timeout, a.err)) {
           ok = false;
           break;
         }
-        bool is_v;
-        int kv_tile;
-        if (!dual) {
-          is_v = (i & 1) != 0;
-          kv_tile = j0 + (i >> 1);
-        } else if (i < 2) {
-          is_v = false;
-          kv_tile = (i == 0) ? j0 : j0b;
-        } else {
-          const int g = (i - 2) >> 2, rr = (i - 2) & 3;
-          if (g == J - 1) {  // last step: Va, Vb
-            is_v = true;
-            kv_tile = (rr == 0 ? j0 : j0b) + g;
+        load_q(u, 0);
+        // Ring order == the MMA warp's consumption order. Normal: K0, V0, K1, V1, ... (each
+        // tile feeds both Q tiles; the next unit's K0 follows this unit's last V). Dual: Ka0,
+        // Kb0, then per step j: Va_j, Ka_j+1, Vb_j, Kb_j+1.
+        const int n_tiles = dual ? 4 * u.J : 2 * u.J;
+        for (int k = 0; k < n_tiles; ++k) {
+          const int st = i % C::STAGES;
+          const uint32_t ph = static_cast<uint32_t>(i / C::STAGES) & 1u;
+          if (!mbar_wait(bar(C::B_KV_EMPTY + st), ph ^ 1u, a.timeout, a.err)) {
+            ok = false;
+            break;
+          }
+          bool is_v;
+          int kv_tile;
+          if (!dual) {
+            is_v = (k & 1) != 0;
+            kv_tile = u.j0 + (k >> 1);
+          } else if (k < 2) {
+            is_v = false;
+            kv_tile = (k == 0) ? u.j0 : u.j0b;
           } else {
-            is_v = (rr & 1) == 0;
-            kv_tile = (rr < 2 ? j0 : j0b) + g + (is_v ? 0 : 1);
+            const int g = (k - 2) >> 2, rr = (k - 2) & 3;
+            if (g == u.J - 1) {  // last step: Va, Vb
+              is_v = true;
+              kv_tile = (rr == 0 ? u.j0 : u.j0b) + g;
+            } else {
+              is_v = (rr & 1) == 0;
+              kv_tile = (rr < 2 ? u.j0 : u.j0b) + g + (is_v ? 0 : 1);
+            }
+          }
+          mbar_arrive_expect_tx(bar(C::B_KV_FULL + st), C::TILE_BYTES);
+          const CUtensorMap* m = is_v ? &tmV : &tmK;
+#pragma unroll
+          for (int c = 0; c < C::CHUNKS; ++c) {
+            tma_load_4d(sbase + C::OFF_KV + st * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
+                        bar(C::B_KV_FULL + st), c * 64, kv_tile * BN, u.hkv, u.b, pol_kv);
+          }
+          ++i;
+          if (k == 0 && !dual) {
+            if (n > 0 &&
+                !mbar_wait(bar(C::B_Q_EMPTY + 1), static_cast<uint32_t>(n - 1) & 1u, a.timeout, a.err)) {
+              ok = false;
+              break;
+            }
+            load_q(u, 1);
           }
         }
-        mbar_arrive_expect_tx(bar(C::B_KV_FULL + st), C::TILE_BYTES);
-        const CUtensorMap* m = is_v ? &tmV : &tmK;
-#pragma unroll
-        for (int c = 0; c < C::CHUNKS; ++c) {
-          tma_load_4d(sbase + C::OFF_KV + st * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
-                      bar(C::B_KV_FULL + st), c * 64, kv_tile * BN, hkv, b, pol_kv);
-        }
-        ++issued;
-        if (i == 0 && !dual) load_q(1);
       }
       // Drain: every TMA write into this CTA's shared memory must land before the CTA
-      // can exit, also when another role gave up early.
-      for (int i = max(0, issued - C::STAGES); i < issued; ++i) {
-        mbar_wait(bar(C::B_KV_FULL + i % C::STAGES), static_cast<uint32_t>(i / C::STAGES) & 1u,
+      // can exit, also when another role gave up early. Loads older than the last STAGES
+      // were consumed (their slots were refilled), so they have landed.
+      for (int d = max(0, i - C::STAGES); d < i; ++d) {
+        mbar_wait(bar(C::B_KV_FULL + d % C::STAGES), static_cast<uint32_t>(d / C::STAGES) & 1u,
                   DEFAULT_TIMEOUT, nullptr);
       }
-      if (q0_issued) mbar_wait(bar(C::B_Q + 0), 0, DEFAULT_TIMEOUT, nullptr);
-      if (issued > 0 && !dual) mbar_wait(bar(C::B_Q + 1), 0, DEFAULT_TIMEOUT, nullptr);
+      if (q_loads0 > 0) mbar_wait(bar(C::B_Q + 0), static_cast<uint32_t>(q_loads0 - 1) & 1u, DEFAULT_TIMEOUT, nullptr);
+      if (q_loads1 > 0) mbar_wait(bar(C::B_Q + 1), static_cast<uint32_t>(q_loads1 - 1) & 1u, DEFAULT_TIMEOUT, nullptr);
     }
   } else if (warp == MMA_WARP) {
     reg_dealloc<REGS_OTHER>();
@@ -397,8 +485,10 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       auto kv_wait = [&](int i) -> bool {
         return mwait(C::B_KV_FULL + i % C::STAGES, static_cast<uint32_t>(i / C::STAGES) & 1u);
       };
+      Unit u;
+      get_unit<CAUSAL>(a, 0, u);
       if (dual) {
-        // Each K/V tile feeds one Q tile; ci walks the ring in the loader's order.
+        // One unit. Each K/V tile feeds one Q tile; ci walks the ring in the loader's order.
         int ci = 0;
         auto take = [&]() -> int {
           const int slot = ci++;
@@ -418,8 +508,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           issue_qk(1, sb);
           mma_commit(bar(C::B_S_FULL + 1));
           mma_commit(bar(C::B_KV_EMPTY + sb));
-          for (int j = 0; j < J; ++j) {
-            const bool more = (j + 1 < J);
+          for (int j = 0; j < u.J; ++j) {
+            const bool more = (j + 1 < u.J);
             const uint32_t pph = static_cast<uint32_t>(j) & 1u;
             for (int t = 0; t < 2; ++t) {
               const int sv = take();
@@ -440,39 +530,60 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           }
         } while (false);
       } else {
-      do {
+        do {
+          // First unit: QK of both tiles on its K_0. Later units' first QKs are issued in the
+          // last step of the unit before, as the next step of one continuous stream.
           if (!mwait(C::B_Q + 0, 0) || !kv_wait(0)) { ok = false; break; }
           tc_fence_after();
           issue_qk(0, 0);
           mma_commit(bar(C::B_S_FULL + 0));
+          if (u.J == 1) mma_commit(bar(C::B_Q_EMPTY + 0));
           if (!mwait(C::B_Q + 1, 0)) { ok = false; break; }
           tc_fence_after();
           issue_qk(1, 0);
           mma_commit(bar(C::B_S_FULL + 1));
           mma_commit(bar(C::B_KV_EMPTY + 0));
-          for (int j = 0; j < J; ++j) {
-            const int iv = 2 * j + 1, ik = 2 * j + 2;
-            const int sv = iv % C::STAGES, sk = ik % C::STAGES;
-            const bool more = (j + 1 < J);
-            const uint32_t pph = static_cast<uint32_t>(j) & 1u;
-            if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
-            if (more) {
-              if (!kv_wait(ik)) { ok = false; break; }
-              tc_fence_after();
-              issue_qk(0, sk);
-              mma_commit(bar(C::B_S_FULL + 0));
-            } else {
-              mma_commit(bar(C::B_O_FULL + 0));
+          if (u.J == 1) mma_commit(bar(C::B_Q_EMPTY + 1));
+          int n = 0, i = 0, g = 0;  // unit, ring position of its K_0, steps of the units before
+          while (true) {
+            Unit nx;
+            const bool has_next = get_unit<CAUSAL>(a, n + 1, nx);
+            const uint32_t qph_next = static_cast<uint32_t>(n + 1) & 1u;
+            for (int j = 0; j < u.J; ++j) {
+              const bool last = (j + 1 == u.J);
+              // V_j, then K_j+1 (at the last step: the next unit's K_0, the next ring entry).
+              const int iv = i + 2 * j + 1, ik = i + 2 * j + 2;
+              const int sv = iv % C::STAGES, sk = ik % C::STAGES;
+              const bool more = !last || has_next;
+              // The QK issued below is its unit's last one for tile t: Q_t may be reloaded after it.
+              const bool qk_final = last ? (has_next && nx.J == 1) : (j + 2 == u.J);
+              const uint32_t pph = static_cast<uint32_t>(g + j) & 1u;
+              if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
+              if (last) mma_commit(bar(C::B_O_FULL + 0));
+              if (more) {
+                if ((last && !mwait(C::B_Q + 0, qph_next)) || !kv_wait(ik)) { ok = false; break; }
+                tc_fence_after();
+                issue_qk(0, sk);
+                mma_commit(bar(C::B_S_FULL + 0));
+                if (qk_final) mma_commit(bar(C::B_Q_EMPTY + 0));
+              }
+              if (!pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
+              mma_commit(bar(C::B_KV_EMPTY + sv));
+              if (last) mma_commit(bar(C::B_O_FULL + 1));
+              if (more) {
+                if (last && !mwait(C::B_Q + 1, qph_next)) { ok = false; break; }
+                tc_fence_after();
+                issue_qk(1, sk);
+                mma_commit(bar(C::B_S_FULL + 1));
+                mma_commit(bar(C::B_KV_EMPTY + sk));
+                if (qk_final) mma_commit(bar(C::B_Q_EMPTY + 1));
+              }
             }
-            if (!pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
-            mma_commit(bar(C::B_KV_EMPTY + sv));
-            if (more) {
-              issue_qk(1, sk);
-              mma_commit(bar(C::B_S_FULL + 1));
-              mma_commit(bar(C::B_KV_EMPTY + sk));
-            } else {
-              mma_commit(bar(C::B_O_FULL + 1));
-            }
+            if (!ok || !has_next) break;
+            i += 2 * u.J;
+            g += u.J;
+            ++n;
+            u = nx;
           }
         } while (false);
       }
@@ -490,190 +601,174 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t tS = tmem + lane_addr + t * BN;
     const uint32_t tP = tS + BN / 2;
     const uint32_t tO = tmem + lane_addr + C::TMEM_O + t * D;
-    const int tile_row0 = row0 + (dual ? 0 : t * BM);  // dual: both tiles hold Q tile 0's rows
-    const int kv_base = (dual && t == 1) ? j0b : j0;   // first K/V tile of this tile's range
-    const int pos = (tile_row0 + r) / a.pack;    // sequence position of this row
-    const int tile_pos0 = tile_row0 / a.pack;    // position of the tile's first row
     const float qk_scale = a.qk_scale;
     const uint64_t sc2 = f2_pack(qk_scale, qk_scale);
+    const uint32_t so = sbase + C::OFF_STG + warp * C::STG_SLOT_BYTES;  // this warp's O staging slot
 
-    float m_use = -INFINITY;  // reference max of this row (scaled, base 2)
-    float l = 0.0f;
-    for (int j = 0; j < J; ++j) {
-      bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(j) & 1u, a.timeout, a.err);
-      if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-      tc_fence_after();
-      const int col0 = (kv_base + j) * BN;
-      const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
-      const bool need_pad = (col0 + BN > a.n_kv);
-      const bool masked = need_causal || need_pad;  // uniform over the warpgroup
-      int lim = a.n_kv - 1 - col0;                  // last visible column of this tile, relative
-      if (CAUSAL) lim = min(lim, pos - col0);
+    int g = 0;  // steps of the units before
+    Unit u;
+    bool have = get_unit<CAUSAL>(a, 0, u);
+    for (int n = 0; ok && have; ++n) {
+      const int J = u.J;
+      const int tile_row0 = u.row0 + (dual ? 0 : t * BM);  // dual: both tiles hold Q tile 0's rows
+      const int kv_base = (dual && t == 1) ? u.j0b : u.j0;  // first K/V tile of this tile's range
+      const int pos = (tile_row0 + r) >> a.pack_shift;      // sequence position of this row
+      const int tile_pos0 = tile_row0 >> a.pack_shift;      // position of the tile's first row
 
-      // The whole S row (128 columns) in one batch of loads and a single wait.
-      uint32_t s[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) mask_chunk(s[c], c * 32, lim);
-      }
-      const float m_cand = fmaxf(row_max64(s[0], s[1]), row_max64(s[2], s[3])) * qk_scale;
-      const bool bump = m_cand > m_use + RESCALE_TH;  // first tile: always (m_use = -inf)
-      float alpha = 1.0f;
-      if (bump) {
-        alpha = ex2_mufu(m_use - m_cand);
-        m_use = m_cand;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, bump)) {
-        // PV(t, j-1) has retired: S_t(j) was committed after it.
-        rescale_o_cols<D>(tO, alpha);
-      }
+      float m_use = -INFINITY;  // reference max of this row (scaled, base 2)
+      float l = 0.0f;
+      for (int j = 0; j < J; ++j) {
+        bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(g + j) & 1u, a.timeout, a.err);
+        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+        tc_fence_after();
+        const int col0 = (kv_base + j) * BN;
+        const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
+        const bool need_pad = (col0 + BN > a.n_kv);
+        const bool masked = need_causal || need_pad;  // uniform over the warpgroup
+        int lim = a.n_kv - 1 - col0;                  // last visible column of this tile, relative
+        if (CAUSAL) lim = min(lim, pos - col0);
 
-      // P = exp2(s * qk_scale - m) into TMEM; the first P_SPLIT chunks are handed to the
-      // MMA warp before the rest are computed, so PV can start on them.
-      if (FA2_SEQ_SOFTMAX) {
-        // Tile 1 computes step j after tile 0's step j; tile 0 computes step j after tile 1's
-        // step j - 1, so the two exp phases of an SMSP do not compete for its XU / FMA pipes.
-        const bool need = (t == 1) || (j > 0);
-        if (need) {
-          const uint32_t par = static_cast<uint32_t>(t == 1 ? j : j - 1) & 1u;
-          bool w2 = mbar_wait(bar(C::B_SEQ + (t ^ 1)), par, a.timeout, a.err);
-          if (!__all_sync(0xffffffffu, w2)) { ok = false; break; }
-        }
-      }
-      // A row that has seen only masked columns so far (possible inside a split) keeps
-      // m_use = -inf; its p must be exactly 0, not exp2(-inf + inf).
-      const float m_safe = (m_use == -INFINITY) ? 0.0f : m_use;
-      const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
-#if FA2_P_ALL_FIRST
-      uint32_t pk[4][16];
+        // The whole S row (128 columns) in one batch of loads and a single wait.
+        uint32_t s[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (masked) {
-          make_p32<BF16, false>(s[c], sc2, nm2, pk[c]);
-        } else {
-          make_p32<BF16, true>(s[c], sc2, nm2, pk[c]);
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_st16(tP + c * 16, pk[c]);
-        if (c == P_SPLIT - 1) {
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(bar(C::B_P_FULL + t));
-        }
-      }
-#else
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-        if (masked) {
-          make_p32<BF16, false>(s[c], sc2, nm2, pk);
-        } else {
-          make_p32<BF16, true>(s[c], sc2, nm2, pk);
-        }
-        tmem_st16(tP + c * 16, pk);
-        if (c == P_SPLIT - 1) {
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(bar(C::B_P_FULL + t));
-        }
-      }
-#endif
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(bar(C::B_P_LATE + t));
-      if (FA2_SEQ_SOFTMAX) mbar_arrive(bar(C::B_SEQ + t));
-
-      // Row sum of the fp32 p (before rounding, as fa2/kernel.py:98), off the critical path.
-      uint64_t acc2[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          acc2[(i >> 1) & 3] =
-              f2_add(acc2[(i >> 1) & 3], f2_pack(__uint_as_float(s[c][i]), __uint_as_float(s[c][i + 1])));
-        }
-      }
-      const uint64_t acc01 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
-      float sl0, sl1;
-      f2_unpack(acc01, sl0, sl1);
-      l = l * alpha + (sl0 + sl1);
-    }
-
-    // ---------------------------------------------------------------- epilogue
-    if (ok) {
-      bool w = mbar_wait(bar(C::B_O_FULL + t), 0, a.timeout, a.err);
-      if (!__all_sync(0xffffffffu, w)) ok = false;
-    }
-    if (ok && a.num_splits > 1) {
-      // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
-      // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
-      tc_fence_after();
-      const bool has = (l > 0.0f);
-      const float inv_l = has ? 1.0f / l : 0.0f;
-      const int split_idx = dual ? 2 * static_cast<int>(blockIdx.z) + t : static_cast<int>(blockIdx.z);
-      const int64_t slot = (static_cast<int64_t>(split_idx) * gridDim.x + blockIdx.x) * a.rows_pad + tile_row0 + r;
-      float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D);
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
         tmem_wait_ld();
-        reg_fence32(o);
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          dst[c * 8 + v] = make_float4(__uint_as_float(o[4 * v]) * inv_l, __uint_as_float(o[4 * v + 1]) * inv_l,
-                                       __uint_as_float(o[4 * v + 2]) * inv_l, __uint_as_float(o[4 * v + 3]) * inv_l);
+        for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
+        if (masked) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) mask_chunk(s[c], c * 32, lim);
         }
-      }
-      a.lse_part[slot] = has ? m_use + log2f(l) : -INFINITY;
-    } else
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = 1.0f / l;
-      const uint32_t so = sbase + C::OFF_Q + t * C::TILE_BYTES;  // Q_t is dead: reuse as staging
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_wait_ld();
-        reg_fence32(o);
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          pk[e] = cvt_pack2<BF16>(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
+        const float m_cand = fmaxf(row_max64(s[0], s[1]), row_max64(s[2], s[3])) * qk_scale;
+        const bool bump = m_cand > m_use + RESCALE_TH;  // first tile: always (m_use = -inf)
+        float alpha = 1.0f;
+        if (bump) {
+          alpha = ex2_mufu(m_use - m_cand);
+          m_use = m_cand;
         }
-        const uint32_t row_addr = so + (c >> 1) * C::CHUNK_BYTES + r * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t unit = static_cast<uint32_t>((c & 1) * 4 + u);
-          st_shared_v4(row_addr + ((unit ^ static_cast<uint32_t>(r & 7)) << 4), pk[4 * u], pk[4 * u + 1],
-                       pk[4 * u + 2], pk[4 * u + 3]);
+        if (j > 0 && __any_sync(0xffffffffu, bump)) {
+          // PV(t, j-1) has retired: S_t(j) was committed after it.
+          rescale_o_cols<D>(tO, alpha);
         }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        const int R0 = tile_row0 + q * 32;
-        const int pos0 = R0 / a.pack;
-        const int h0 = hq0 + R0 % a.pack;
-        if (pos0 < a.n_q) {
+
+        // P = exp2(s * qk_scale - m) into TMEM; the first P_SPLIT chunks are handed to the
+        // MMA warp before the rest are computed, so PV can start on them.
+        // A row that has seen only masked columns so far (possible inside a split) keeps
+        // m_use = -inf; its p must be exactly 0, not exp2(-inf + inf).
+        const float m_safe = (m_use == -INFINITY) ? 0.0f : m_use;
+        const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
 #pragma unroll
-          for (int c = 0; c < C::CHUNKS; ++c) {
-            tma_store_4d(&tmO, so + c * C::CHUNK_BYTES + q * 32 * 128, c * 64, h0, pos0, b);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+          if (masked) {
+            make_p32<BF16, false>(s[c], sc2, nm2, pk);
+          } else {
+            make_p32<BF16, true>(s[c], sc2, nm2, pk);
           }
-          bulk_commit();
-          bulk_wait_all();
+          tmem_st16(tP + c * 16, pk);
+          if (c == P_SPLIT - 1) {
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar(C::B_P_FULL + t));
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(C::B_P_LATE + t));
+
+        // Row sum of the fp32 p (before rounding, as fa2/kernel.py:98), off the critical path.
+        uint64_t acc2[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            acc2[(i >> 1) & 3] =
+                f2_add(acc2[(i >> 1) & 3], f2_pack(__uint_as_float(s[c][i]), __uint_as_float(s[c][i + 1])));
+          }
+        }
+        const uint64_t acc01 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
+        float sl0, sl1;
+        f2_unpack(acc01, sl0, sl1);
+        l = l * alpha + (sl0 + sl1);
+      }
+      if (!ok) break;
+      g += J;
+      // The next unit, decoded while PV(t, J - 1) runs.
+      Unit nu;
+      have = get_unit<CAUSAL>(a, n + 1, nu);
+
+      // -------------------------------------------------------------- epilogue
+      {
+        bool w = mbar_wait(bar(C::B_O_FULL + t), static_cast<uint32_t>(n) & 1u, a.timeout, a.err);
+        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+      }
+      tc_fence_after();
+      if (a.num_splits > 1) {
+        // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
+        // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
+        const bool has = (l > 0.0f);
+        const float inv_l = has ? 1.0f / l : 0.0f;
+        const int split_idx = dual ? 2 * static_cast<int>(blockIdx.z) + t : static_cast<int>(blockIdx.z);
+        const int64_t slot = (static_cast<int64_t>(split_idx) * gridDim.x + u.x) * a.rows_pad + tile_row0 + r;
+        float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D);
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            dst[c * 8 + v] = make_float4(__uint_as_float(o[4 * v]) * inv_l, __uint_as_float(o[4 * v + 1]) * inv_l,
+                                         __uint_as_float(o[4 * v + 2]) * inv_l, __uint_as_float(o[4 * v + 3]) * inv_l);
+          }
+        }
+        a.lse_part[slot] = has ? m_use + log2f(l) : -INFINITY;
+      } else {
+        // O / l in the input dtype, 64 columns at a time through this warp's staging slot and
+        // one TMA store per chunk. Lane 0 issued every store from the slot, so it alone waits
+        // for the slot to have been read before it is rewritten (the next chunk's conversion
+        // overlaps the read).
+        uint32_t o[D / 32][32];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + c * 32, o[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) reg_fence32(o[c]);
+        const float inv_l = 1.0f / l;
+        const uint64_t inv2 = f2_pack(inv_l, inv_l);
+        const int R0 = tile_row0 + q * 32;  // first row of this warp
+        const int pos0 = R0 >> a.pack_shift;
+        const int h0 = u.hq0 + (R0 & (a.pack - 1));
+#pragma unroll
+        for (int ch = 0; ch < C::CHUNKS; ++ch) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const uint32_t* src = o[2 * ch + (e >> 4)];
+            float x0, x1;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(src[(2 * e) & 31]), __uint_as_float(src[(2 * e + 1) & 31])), inv2),
+                      x0, x1);
+            pk[e] = cvt_pack2<BF16>(x0, x1);
+          }
+          if (lane == 0) bulk_wait_read();
+          __syncwarp();
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            st_shared_v4(so + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
+                         pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && pos0 < a.n_q) {
+            tma_store_4d(&tmO, so, ch * 64, h0, pos0, u.b);
+            bulk_commit();
+          }
         }
       }
-      __syncwarp();
+      u = nu;
     }
+    if (lane == 0) bulk_wait_all();  // the last stores have read the slot and written O
   } else {
     reg_dealloc<REGS_OTHER>();  // warps 10-11: nothing to do
   }
@@ -693,7 +788,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // One warp per packed row: O = sum_s w_s O_s / sum_s w_s with w_s = 2^(lse_s - max lse), over
 // the splits that cover this row's 256-row block, written in the input dtype with o's strides.
 struct CombineArgs {
-  int n_q, n_kv, pack, hblocks, rows_pad, num_splits, split_tiles;
+  int n_q, n_kv, pack, pack_shift, hblocks, rows_pad, num_splits, split_tiles;
   int64_t ob, oh, on;  // output element strides (b, h, n); d stride is 1
 };
 
@@ -708,7 +803,7 @@ fa2_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l
   const int b = x / c.hblocks;
   const int h = (x % c.hblocks) * c.pack + R % c.pack;
   const int pos = R / c.pack;
-  const int J_cta = cta_kv_tiles<CAUSAL>(R / 256, c.n_q, c.n_kv, c.pack);
+  const int J_cta = cta_kv_tiles<CAUSAL>(R / 256, c.n_q, c.n_kv, c.pack_shift);
   const int ns = min(c.num_splits, (J_cta + c.split_tiles - 1) / c.split_tiles);
   const int64_t xs = static_cast<int64_t>(gridDim.y);
   float mx = -INFINITY;
@@ -786,6 +881,18 @@ bool make_map(CUtensorMap* m, bool bf16, const void* base, const int64_t dims[4]
 
 constexpr int kMaxDevices = 64;
 
+// Streaming multiprocessors of a device (cached; 148 on B200). 0 on error.
+int num_sms(int device) {
+  static int cache[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) return 0;
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
 struct SplitPlan {
   int num_splits = 1, split_tiles = 0, rows_pad = 0, xblocks = 0, dual = 0, grid_z = 1;
   int64_t bytes = 0;
@@ -852,6 +959,8 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.n_kv = p->seqlen_kv;
   ka.group = group;
   ka.pack = pack;
+  ka.pack_shift = 0;
+  while ((1 << ka.pack_shift) < pack) ++ka.pack_shift;  // pack divides 128: a power of two
   ka.hblocks = p->heads_q / pack;
   ka.qk_scale = p->qk_scale;
   ka.err = p->err_flag;
@@ -872,9 +981,22 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   }
 
   const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
-  const dim3 grid(static_cast<unsigned>(static_cast<int64_t>(p->batch) * ka.hblocks),
-                  static_cast<unsigned>((rows + fa2::Q_TILES * fa2::BM - 1) / (fa2::Q_TILES * fa2::BM)),
-                  static_cast<unsigned>(sp.grid_z));
+  const int64_t xblocks = static_cast<int64_t>(p->batch) * ka.hblocks;
+  const int64_t mblocks = (rows + fa2::Q_TILES * fa2::BM - 1) / (fa2::Q_TILES * fa2::BM);
+  const int64_t units = xblocks * mblocks;
+  ka.xblocks = static_cast<int>(xblocks);
+  ka.div_xblocks = fa2::make_fastdiv(static_cast<uint32_t>(xblocks));
+  ka.div_hblocks = fa2::make_fastdiv(static_cast<uint32_t>(ka.hblocks));
+  ka.div_group = fa2::make_fastdiv(static_cast<uint32_t>(group));
+  ka.mblocks = static_cast<int>(mblocks);
+  ka.persistent = (FA2_PERSISTENT && sp.num_splits <= 1 && units <= 0x7fffffffLL) ? 1 : 0;
+  ka.num_units = ka.persistent ? static_cast<int>(units) : 0;
+  dim3 grid(static_cast<unsigned>(xblocks), static_cast<unsigned>(mblocks), static_cast<unsigned>(sp.grid_z));
+  if (ka.persistent) {
+    const int sms = num_sms(device);
+    if (sms <= 0) return FA2_ERR_DEVICE;
+    grid = dim3(static_cast<unsigned>(units < sms ? units : sms), 1, 1);  // one CTA per SM
+  }
   kern<<<grid, fa2::NUM_THREADS, C::SMEM_ALLOC, stream>>>(tmQ, tmK, tmV, tmO, ka);
   if (cudaGetLastError() != cudaSuccess) return FA2_ERR_LAUNCH;
   if (sp.num_splits > 1) {
@@ -882,6 +1004,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
     ca.n_q = p->seqlen_q;
     ca.n_kv = p->seqlen_kv;
     ca.pack = pack;
+    ca.pack_shift = ka.pack_shift;
     ca.hblocks = ka.hblocks;
     ca.rows_pad = sp.rows_pad;
     ca.num_splits = sp.num_splits;
