@@ -1,0 +1,147 @@
+"""Design-choice ablation: each choice of the sm_100a kernel against its alternative, timed
+on the BASELINE configs (the role of the reference's bench/ablation.py).
+
+Every variant computes the full attention (no work is skipped); they differ only in how:
+
+  shipped        the library as built by build.py
+  no_persistent  one CTA per 256-row work unit (FA2_PERSISTENT=0) instead of one CTA per SM
+                 walking the units
+  all_mufu       every exp2 on the MUFU (FA2_EMU_MASK=0) instead of 25% on the FMA pipe
+  emu_50         half of the exp2 on the FMA pipe (FA2_EMU_MASK=0x5555)
+  p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
+  pack_on        (runtime) GQA head packing forced on, on the pack_tail config (the packing rule
+                 leaves it off there: 0.977 vs 0.992 tile fill)
+  splitkv_off    (runtime) split-KV off (num_splits=1), on the decode config
+
+    python triton-fa2-forward_b200/ablation.py [--variants shipped,all_mufu] [--configs headline]
+
+Variant libraries are compiled into triton-fa2-forward_b200/_build/ablation/ and each runs in a
+child process. Timing: 3 warm-up calls, then the median of 20 calls with a 256 MiB L2 flush
+before each, CUDA events on the current stream. Prints one JSON line per (variant, config).
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, PKG_DIR)
+
+import build as fa2_build  # noqa: E402
+
+BUILD_DIR = os.path.join(PKG_DIR, "_build", "ablation")
+
+COMPILED = {
+    "shipped": [],
+    "no_persistent": ["-DFA2_PERSISTENT=0"],
+    "all_mufu": ["-DFA2_EMU_MASK=0x0u"],
+    "emu_50": ["-DFA2_EMU_MASK=0x5555u"],
+    "p_split_2": ["-DFA2_P_SPLIT=2"],
+}
+RUNTIME = {
+    # name: (library variant, config it applies to, attention() keyword arguments)
+    "pack_on": ("shipped", "pack_tail", {"pack_gqa": True}),
+    "splitkv_off": ("shipped", "decode", {"num_splits": 1}),
+}
+
+
+def lib_path(name):
+    return os.path.join(BUILD_DIR, f"libfa2_sm100_{name}.so")
+
+
+def build_variant(name):
+    """Compile one variant library (skipped when it is newer than every source)."""
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    out = lib_path(name)
+    if fa2_build.up_to_date(out=out):
+        return out
+    cmd = [fa2_build.nvcc_path(), *fa2_build.NVCC_FLAGS, *COMPILED[name], "-I", fa2_build.INCLUDE,
+           "-I", fa2_build.CSRC, "-o", out, *fa2_build.SOURCES]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {name}:\n{res.stderr}")
+    return out
+
+
+def child(lib, config, kwargs_json):
+    """Runs in a fresh process: time `config` with library `lib`, print one JSON line."""
+    from fa2 import _lib
+
+    _lib.LIB_PATH = lib
+    import torch
+
+    from fa2.kernel import attention, check_device_errors
+    from profile_target import CONFIGS as SHAPES
+
+    kwargs = json.loads(kwargs_json)
+    B, Hq, Hkv, N, D, dt, causal, scale = SHAPES[config]
+    n_q, n_kv = N if isinstance(N, tuple) else (N, N)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, Hq, n_q, D, device="cuda", dtype=dt, generator=g) * scale
+    k = torch.randn(B, Hkv, n_kv, D, device="cuda", dtype=dt, generator=g) * scale
+    v = torch.randn(B, Hkv, n_kv, D, device="cuda", dtype=dt, generator=g) * scale
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(3):
+        attention(q, k, v, causal=causal, **kwargs)
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(20):
+        flush.fill_(1)
+        torch.cuda._sleep(200_000)  # keeps the stream ahead of the host's launch
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        attention(q, k, v, causal=causal, **kwargs)
+        e.record()
+        torch.cuda.synchronize()
+        ts.append(s.elapsed_time(e))
+    check_device_errors()
+    ts.sort()
+    ms = ts[len(ts) // 2]
+    pairs = n_q * (n_q + 1) / 2 if causal else n_q * n_kv
+    tflops = 4 * B * Hq * pairs * D / (ms * 1e-3) / 1e12
+    nbytes = (q.numel() * 2 + k.numel() + v.numel()) * q.element_size()
+    print(json.dumps({"config": config, "ms": ms, "tflops": tflops,
+                      "gbs": nbytes / (ms * 1e-3) / 1e9, "iqr_ms": ts[15] - ts[5]}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--variants", default=",".join(list(COMPILED) + list(RUNTIME)))
+    ap.add_argument("--configs", default="headline,mha_causal,full_long")
+    ap.add_argument("--child", nargs=3, metavar=("LIB", "CONFIG", "KWARGS"))
+    ap.add_argument("--build-only", action="store_true")
+    args = ap.parse_args()
+    if args.child:
+        child(*args.child)
+        return 0
+    variants = [v for v in args.variants.split(",") if v]
+    for v in variants:
+        build_variant(RUNTIME[v][0] if v in RUNTIME else v)
+    if args.build_only:
+        return 0
+    rc = 0
+    for v in variants:
+        if v in RUNTIME:
+            libname, cfg, kw = RUNTIME[v]
+            runs = [("shipped", cfg, {}), (v, cfg, kw)]
+        else:
+            libname = v
+            runs = [(v, c, {}) for c in args.configs.split(",") if c]
+        for name, cfg, kw in runs:
+            res = subprocess.run([sys.executable, os.path.abspath(__file__), "--child", lib_path(libname), cfg,
+                                  json.dumps(kw)], capture_output=True, text=True, timeout=600)
+            line = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+            if res.returncode != 0 or not line:
+                print(json.dumps({"variant": name, "config": cfg, "error": res.stderr[-400:]}), flush=True)
+                rc = 1
+                continue
+            d = json.loads(line[0])
+            d["variant"] = name
+            print(json.dumps(d), flush=True)
+    return rc
+
+
+if __name__ == "__main__":
+    sys.exit(main())

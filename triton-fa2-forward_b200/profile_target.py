@@ -3,6 +3,7 @@ launch(es) a profiler captures (e.g. `ncu -k regex:fa2_fwd -s <warmup> -c 1`).
 Mirrors the role of the reference's bench/profile_target.py.
 
     python triton-fa2-forward_b200/profile_target.py [--config headline] [--warmup 2] [--launches 1]
+        [--lib path/to/libfa2_sm100_variant.so]   (a library built by ablation.py)
 
 Configs are the BASELINE.json shapes; inputs are seeded N(0,1) generated on the device.
 The headline config holds 470 MB (inputs 335 MB > 126 MB L2), so DRAM counters are meaningful.
@@ -15,8 +16,6 @@ import sys
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 import torch  # noqa: E402
-
-from fa2.kernel import attention, check_device_errors  # noqa: E402
 
 CONFIGS = {
     "plumbing": (1, 2, 2, 256, 64, torch.float16, True, 1.0),
@@ -35,7 +34,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--launches", type=int, default=1)
     ap.add_argument("--pack", choices=["auto", "on", "off"], default="auto")
+    ap.add_argument("--lib", default=None, help="load this build of libfa2_sm100.so instead of the shipped one")
     args = ap.parse_args()
+    if args.lib:
+        from fa2 import _lib
+        _lib.LIB_PATH = os.path.abspath(args.lib)
+    from fa2.kernel import attention, check_device_errors
     B, Hq, Hkv, N, D, dt, causal, scale = CONFIGS[args.config]
     n_q, n_kv = N if isinstance(N, tuple) else (N, N)
     g = torch.Generator(device="cuda").manual_seed(0)
