@@ -6,11 +6,13 @@ Every variant computes the full attention (no work is skipped); they differ only
   shipped        the library as built by build.py
   no_persistent  one CTA per 256-row work unit (FA2_PERSISTENT=0) instead of one CTA per SM
                  walking the units
-  all_mufu       every exp2 on the MUFU (FA2_EMU_MASK=0) instead of 25% on the FMA pipe
-  emu_50         half of the exp2 on the FMA pipe (FA2_EMU_MASK=0x5555)
+  all_mufu       every exp2 on the MUFU (shipped: 25% on the FMA pipe at D=128, none at D=64)
+  emu_25         25% of the exp2 on the FMA pipe at both head dims
+  emu_50         half of the exp2 on the FMA pipe at both head dims
   p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
-  pack_on        (runtime) GQA head packing forced on, on the pack_tail config (the packing rule
-                 leaves it off there: 0.977 vs 0.992 tile fill)
+  pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
+                 packs whenever the group divides 128; the reference's rule would not pack here)
+  pack_off_headline, pack_off_mqa   the same on the headline and on an MQA shape
   splitkv_off    (runtime) split-KV off (num_splits=1), on the decode config
 
     python triton-fa2-forward_b200/ablation.py [--variants shipped,all_mufu] [--configs headline]
@@ -36,13 +38,16 @@ BUILD_DIR = os.path.join(PKG_DIR, "_build", "ablation")
 COMPILED = {
     "shipped": [],
     "no_persistent": ["-DFA2_PERSISTENT=0"],
-    "all_mufu": ["-DFA2_EMU_MASK=0x0u"],
-    "emu_50": ["-DFA2_EMU_MASK=0x5555u"],
+    "all_mufu": ["-DFA2_EMU_MASK_D128=0x0u", "-DFA2_EMU_MASK_D64=0x0u"],
+    "emu_25": ["-DFA2_EMU_MASK_D128=0x2222u", "-DFA2_EMU_MASK_D64=0x2222u"],
+    "emu_50": ["-DFA2_EMU_MASK_D128=0x5555u", "-DFA2_EMU_MASK_D64=0x5555u"],
     "p_split_2": ["-DFA2_P_SPLIT=2"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)
-    "pack_on": ("shipped", "pack_tail", {"pack_gqa": True}),
+    "pack_off": ("shipped", "pack_tail", {"pack_gqa": False}),
+    "pack_off_headline": ("shipped", "headline", {"pack_gqa": False}),
+    "pack_off_mqa": ("shipped", "mqa_causal", {"pack_gqa": False}),
     "splitkv_off": ("shipped", "decode", {"num_splits": 1}),
 }
 

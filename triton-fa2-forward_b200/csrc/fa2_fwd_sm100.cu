@@ -67,8 +67,15 @@ constexpr int REGS_SOFTMAX = 200;
 constexpr int REGS_OTHER = 104;
 constexpr float RESCALE_TH = 8.0f;               // log2 units: P may reach 2^8 before a rescale
 constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
-#ifndef FA2_EMU_MASK
-#define FA2_EMU_MASK 0x2222u  // pairs 1,5,9,13 of every 16: 25% of the exp2 on the FMA pipe
+// Which of the 16 exp2 pairs of a 32-column chunk run on the FMA pipe (the rest on the MUFU).
+// D = 128: pairs 1, 5, 9, 13, i.e. 25% on the FMA pipe. D = 64: none. Each has half the
+// tensor work per score and less pipe headroom for the polynomial; measured all-MUFU
+// +0.6..3.5% at D = 64, -1..2% at D = 128.
+#ifndef FA2_EMU_MASK_D128
+#define FA2_EMU_MASK_D128 0x2222u
+#endif
+#ifndef FA2_EMU_MASK_D64
+#define FA2_EMU_MASK_D64 0x0u
 #endif
 #ifndef FA2_P_SPLIT
 #define FA2_P_SPLIT 3  // P chunks (of 32 columns) handed to the MMA warp before the rest
@@ -79,7 +86,10 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
 #endif
-constexpr uint32_t EMU_PAIR_MASK = FA2_EMU_MASK;
+template <int D>
+__host__ __device__ constexpr uint32_t emu_pair_mask() {
+  return D == 128 ? static_cast<uint32_t>(FA2_EMU_MASK_D128) : static_cast<uint32_t>(FA2_EMU_MASK_D64);
+}
 constexpr int P_SPLIT = FA2_P_SPLIT;
 static_assert(P_SPLIT >= 1 && P_SPLIT <= 3, "P hand-off split");
 // setmaxnreg draws on the registers the CTA was launched with (384 threads x 168).
@@ -252,16 +262,16 @@ __device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], int c0, int lim) {
 }
 
 // p = exp2(s * scale - m) for 32 scores: packed to 16 words of (lo, hi) halves for the PV
-// GEMM, and written back into s as fp32 for the row sum. EMU: a fixed subset of pairs is
+// GEMM, and written back into s as fp32 for the row sum. The pairs set in EMU_MASK are
 // computed on the FMA pipe (exp2_poly_x2); the subset depends only on the column index.
-template <bool BF16, bool EMU>
+template <bool BF16, uint32_t EMU_MASK>
 __device__ __forceinline__ void make_p32(uint32_t (&s)[32], uint64_t sc2, uint64_t nm2, uint32_t (&pk)[16]) {
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
     const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), sc2, nm2);
     float x0, x1, p0, p1;
     f2_unpack(x2, x0, x1);
-    if (EMU && ((EMU_PAIR_MASK >> e) & 1u)) {
+    if ((EMU_MASK >> e) & 1u) {
       exp2_poly_x2<BF16 ? 3 : 4>(x0, x1, p0, p1);
     } else {
       p0 = ex2_mufu(x0);
@@ -661,9 +671,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
           if (masked) {
-            make_p32<BF16, false>(s[c], sc2, nm2, pk);
+            make_p32<BF16, 0u>(s[c], sc2, nm2, pk);
           } else {
-            make_p32<BF16, true>(s[c], sc2, nm2, pk);
+            make_p32<BF16, emu_pair_mask<D>()>(s[c], sc2, nm2, pk);
           }
           tmem_st16(tP + c * 16, pk);
           if (c == P_SPLIT - 1) {

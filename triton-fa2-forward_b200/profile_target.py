@@ -25,6 +25,10 @@ CONFIGS = {
     "pack_tail": (16, 64, 8, 1000, 128, torch.bfloat16, True, 1.0),
     # short query against a long K/V (decode): HBM-bound, GQA-packed, split-KV in pairs
     "decode": (4, 32, 8, (1, 65536), 128, torch.bfloat16, False, 1.0),
+    # the other dtype at each head dim (design-choice ablation)
+    "mha_causal_fp16": (4, 16, 16, 4096, 128, torch.float16, True, 1.0),
+    "full_long_bf16": (2, 32, 32, 16384, 64, torch.bfloat16, False, 0.5),
+    "mqa_causal": (2, 32, 1, 4096, 128, torch.bfloat16, True, 1.0),
 }
 
 
