@@ -10,6 +10,8 @@ Every variant computes the full attention (no work is skipped); they differ only
   emu_25         25% of the exp2 on the FMA pipe at both head dims
   emu_50         half of the exp2 on the FMA pipe at both head dims
   p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
+  qk_split       QK issued as two N=64 halves, the first before PV has read P (FA2_QK_SPLIT=1),
+                 instead of one N=128 GEMM after PV
   pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
                  packs whenever the group divides 128; the reference's rule would not pack here)
   pack_off_headline, pack_off_mqa   the same on the headline and on an MQA shape
@@ -42,6 +44,7 @@ COMPILED = {
     "emu_25": ["-DFA2_EMU_MASK_D128=0x2222u", "-DFA2_EMU_MASK_D64=0x2222u"],
     "emu_50": ["-DFA2_EMU_MASK_D128=0x5555u", "-DFA2_EMU_MASK_D64=0x5555u"],
     "p_split_2": ["-DFA2_P_SPLIT=2"],
+    "qk_split": ["-DFA2_QK_SPLIT=1"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

@@ -83,6 +83,13 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_MMA_SPIN
 #define FA2_MMA_SPIN 0  // 1: the MMA thread polls its barriers without suspending (measured: no gain)
 #endif
+#ifndef FA2_QK_SPLIT
+// 1: each QK GEMM is issued as two N = 64 halves. The half writing S columns 0-63 does not
+// touch P (columns 64-127), so it is issued right after the first part of the previous PV.
+// Measured 22% slower at the headline (the second operand read twice, N = 64 MMAs, and the low
+// half queued ahead of the rest of PV); kept as an ablation alternative.
+#define FA2_QK_SPLIT 0
+#endif
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
 #endif
@@ -469,6 +476,18 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           mma_ss(tmem + t * BN, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
+      // QK of tile t, score columns [64 h, 64 h + 64) only: K rows 64 h .. 64 h + 63, which sit
+      // 8 KiB into each 16 KiB swizzle chunk of the K tile.
+      constexpr uint32_t idesc_qk64 = idesc_f16(BF16, BM, BN / 2, false);
+      auto issue_qk_half = [&](int t, int st, int h) {
+        const uint64_t qd = dq_base + static_cast<uint64_t>((t * C::TILE_BYTES) >> 4);
+        const uint64_t kd = dk_base + static_cast<uint64_t>((st * C::TILE_BYTES + h * (BN / 2) * 128) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * C::CHUNK_BYTES + (kk & 3) * 32) >> 4);
+          mma_ss(tmem + t * BN + h * (BN / 2), qd + off, kd + off, idesc_qk64, kk > 0 ? 1u : 0u);
+        }
+      };
       auto issue_pv = [&](int t, int st, bool acc, int kk0, int kk1) {
         const uint64_t vd = dv_base + static_cast<uint64_t>((st * C::TILE_BYTES) >> 4);
 #pragma unroll
@@ -568,6 +587,33 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
               // The QK issued below is its unit's last one for tile t: Q_t may be reloaded after it.
               const bool qk_final = last ? (has_next && nx.J == 1) : (j + 2 == u.J);
               const uint32_t pph = static_cast<uint32_t>(g + j) & 1u;
+#if FA2_QK_SPLIT
+              // Per tile: PV part 1, QK low half (S columns 0-63; the softmax has read S, as its
+              // P_FULL arrival shows), PV part 2, QK high half (after PV has read P).
+              if (!kv_wait(iv)) { ok = false; break; }
+              for (int t = 0; t < 2; ++t) {
+                if (!mwait(C::B_P_FULL + t, pph)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv(t, sv, j > 0, 0, 2 * P_SPLIT);
+                if (more) {
+                  if ((last && !mwait(C::B_Q + t, qph_next)) || (t == 0 && !kv_wait(ik))) { ok = false; break; }
+                  tc_fence_after();
+                  issue_qk_half(t, sk, 0);
+                }
+                if (!mwait(C::B_P_LATE + t, pph)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv(t, sv, j > 0, 2 * P_SPLIT, BN / 16);
+                if (t == 1) mma_commit(bar(C::B_KV_EMPTY + sv));
+                if (last) mma_commit(bar(C::B_O_FULL + t));
+                if (more) {
+                  issue_qk_half(t, sk, 1);
+                  mma_commit(bar(C::B_S_FULL + t));
+                  if (t == 1) mma_commit(bar(C::B_KV_EMPTY + sk));
+                  if (qk_final) mma_commit(bar(C::B_Q_EMPTY + t));
+                }
+              }
+              if (!ok) break;
+#else
               if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
               if (last) mma_commit(bar(C::B_O_FULL + 0));
               if (more) {
@@ -588,6 +634,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 mma_commit(bar(C::B_KV_EMPTY + sk));
                 if (qk_final) mma_commit(bar(C::B_Q_EMPTY + 1));
               }
+#endif
             }
             if (!ok || !has_next) break;
             i += 2 * u.J;
