@@ -331,11 +331,12 @@ def run_ours(args, world, rank, local):
 
         # ---- device-timed region
         barrier()
-        # A short device-side spin (outside every event pair) keeps the stream busy while the
-        # host enqueues the first steps, so the first pair does not time the host's launch
-        # latency (Python wrapper + ctypes call) as idle GPU time.
-        if hasattr(torch.cuda, "_sleep"):
-            torch.cuda._sleep(4_000_000)  # ~2 ms of SM clocks
+        # One untimed step after the barrier (outside every event pair) brings the GPU back from
+        # the barrier's idle gap and keeps the stream busy while the host enqueues the first
+        # timed steps, so the first pair times neither the host's launch latency (Python
+        # wrapper + ctypes call) nor a clock ramp as kernel time.
+        flush.fill_(1)
+        step()
         for s, e in ev:
             flush.fill_(1)
             s.record()
