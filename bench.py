@@ -464,7 +464,8 @@ def run_ours(args, world, rank, local):
                      "frac": per_gpu_achieved / peak, "peak_source": peak_src,
                      "traffic": profile_traffic(),
                      "algorithmic": f"{rank_flops:.4e} FLOP per launch (4*Hq*D*N(N+1)/2 over the rank's units)"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps,  # one per timed step, each inside its event pair
+        "untimed_launches_after_barrier": 1,
         "clocks": clocks,
         "ms_samples": {"min": min(ms), "median": statistics.median(ms), "max": max(ms),
                        "first": ms[0], "slowest_step": ms.index(max(ms))},
