@@ -166,3 +166,31 @@ def test_auto_num_splits():
     assert auto_num_splits(4, 32, 1, 65536, 4, 4, False) == 8           # 32 CTAs -> 4 pairs each
     assert auto_num_splits(2, 8, 200, 8192, 1, 1, False) == 9           # 200 rows (no pairs): 16 CTAs -> 144
     assert auto_num_splits(1, 8, 1, 512, 8, 8, False) == 1              # too few K/V tiles
+
+
+def test_ablation_switches_exist_in_the_kernel_source():
+    """Every compile-time switch the design-choice ablation passes is a macro the kernel source
+    actually tests, so a renamed switch cannot silently build the shipped kernel twice."""
+    import re
+
+    import ablation
+    import build as fa2_build
+
+    src = "".join(open(p).read() for p in fa2_build.SOURCES)
+    for name, flags in ablation.COMPILED.items():
+        for f in flags:
+            macro = re.match(r"-D(\w+)=", f).group(1)
+            assert f"#ifndef {macro}" in src, (name, macro)
+    for name, (lib, cfg, kwargs) in ablation.RUNTIME.items():
+        assert lib in ablation.COMPILED
+        assert set(kwargs) <= {"pack_gqa", "num_splits"}
+
+
+def test_profile_target_configs_cover_the_ablation():
+    import ablation
+    from profile_target import CONFIGS
+
+    for _, (_, cfg, _) in ablation.RUNTIME.items():
+        assert cfg in CONFIGS
+    for cfg in ("headline", "mha_causal", "full_long", "pack_tail", "decode"):
+        assert cfg in CONFIGS
