@@ -331,10 +331,13 @@ def run_ours(args, world, rank, local):
 
         # ---- device-timed region
         barrier()
-        # One untimed step after the barrier (outside every event pair) brings the GPU back from
-        # the barrier's idle gap and keeps the stream busy while the host enqueues the first
-        # timed steps, so the first pair times neither the host's launch latency (Python
-        # wrapper + ctypes call) nor a clock ramp as kernel time.
+        # A ~1 ms device spin and one untimed step after the barrier (both outside every event
+        # pair) keep the stream ahead of the host and bring the GPU back from the barrier's idle
+        # gap, so the first pair times neither the host's launch latency (Python wrapper + ctypes
+        # call; with N ranks sharing the host cores it can exceed a short per-rank kernel) nor a
+        # clock ramp as kernel time.
+        if hasattr(torch.cuda, "_sleep"):
+            torch.cuda._sleep(2_000_000)
         flush.fill_(1)
         step()
         for s, e in ev:
@@ -467,7 +470,7 @@ def run_ours(args, world, rank, local):
                      "traffic": profile_traffic(),
                      "algorithmic": f"{rank_flops:.4e} FLOP per launch (4*Hq*D*N(N+1)/2 over the rank's units)"},
         "gpu_launches": args.steps,  # one per timed step, each inside its event pair
-        "untimed_launches_after_barrier": 1,
+        "untimed_launches_after_barrier": 1,  # plus a device spin (torch.cuda._sleep)
         "clocks": clocks,
         "ms_samples": {"min": min(ms), "median": statistics.median(ms), "max": max(ms),
                        "first": ms[0], "slowest_step": ms.index(max(ms))},
