@@ -83,6 +83,12 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_MMA_SPIN
 #define FA2_MMA_SPIN 0  // 1: the MMA thread polls its barriers without suspending (measured: no gain)
 #endif
+#ifndef FA2_SPEC_MAX
+// 1: on unmasked steps with a finite reference max, P is computed with the current reference
+// max while the row max is taken; a row whose max moves past the threshold (rare after the
+// first tile) redoes its P before the hand-off. Same values as taking the max first.
+#define FA2_SPEC_MAX 1
+#endif
 #ifndef FA2_QK_SPLIT
 // 1: each QK GEMM is issued as two N = 64 halves. The half writing S columns 0-63 does not
 // touch P (columns 64-127), so it is issued right after the first part of the previous PV.
@@ -290,11 +296,32 @@ __device__ __forceinline__ void make_p32(uint32_t (&s)[32], uint64_t sc2, uint64
   }
 }
 
+// As make_p32, but s keeps the scores (a redo may need them) and the fp32 p are added into the
+// row-sum accumulators instead: pair e goes to acc2[e % 4], the order make_p32's caller sums in.
+template <bool BF16, uint32_t EMU_MASK>
+__device__ __forceinline__ void make_p32_sum(const uint32_t (&s)[32], uint64_t sc2, uint64_t nm2, uint32_t (&pk)[16],
+                                             uint64_t (&acc2)[4]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), sc2, nm2);
+    float x0, x1, p0, p1;
+    f2_unpack(x2, x0, x1);
+    if ((EMU_MASK >> e) & 1u) {
+      exp2_poly_x2<BF16 ? 3 : 4>(x0, x1, p0, p1);
+    } else {
+      p0 = ex2_mufu(x0);
+      p1 = ex2_mufu(x1);
+    }
+    pk[e] = cvt_pack2<BF16>(p0, p1);
+    acc2[e & 3] = f2_add(acc2[e & 3], f2_pack(p0, p1));
+  }
+}
+
 // O row *= alpha for this thread's NCOL columns of O_t (its TMEM lane), 16 at a time.
 template <int NCOL>
 __device__ __forceinline__ void rescale_o_cols(uint32_t tO, float alpha) {
   const uint64_t a2 = f2_pack(alpha, alpha);
-#pragma unroll
+#pragma unroll 1  // rare path: kept rolled, which keeps the unmasked step free of spills
   for (int c = 0; c < NCOL / 16; ++c) {
     uint32_t o[16];
     tmem_ld16(tO + c * 16, o);
@@ -692,6 +719,54 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
+        if (FA2_SPEC_MAX && !masked && j > 0 && __all_sync(0xffffffffu, m_use != -INFINITY)) {
+          // P with the current reference max while the row max is taken (the two are independent
+          // and use different pipes); the threshold test then runs before the hand-off.
+          const float m_cand = fmaxf(row_max64(s[0], s[1]), row_max64(s[2], s[3])) * qk_scale;
+          uint64_t nm2 = f2_pack(-m_use, -m_use);
+          uint64_t acc2[4];
+          float alpha = 1.0f;
+          // Pass 0 uses the current reference max. If some row's max moved past the threshold
+          // (rare), pass 1 moves it, rescales O_t (PV(t, j-1) has retired: S_t(j) was committed
+          // after it) and redoes these chunks with the new reference max.
+#pragma unroll 1
+          for (int pass = 0;; ++pass) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc2[i] = 0;
+#pragma unroll
+            for (int c = 0; c < P_SPLIT; ++c) {
+              uint32_t pk[16];
+              make_p32_sum<BF16, emu_pair_mask<D>()>(s[c], sc2, nm2, pk, acc2);
+              tmem_st16(tP + c * 16, pk);
+            }
+            if (pass == 1) break;
+            const bool bump = m_cand > m_use + RESCALE_TH;
+            if (!__any_sync(0xffffffffu, bump)) break;
+            if (bump) {
+              alpha = ex2_mufu(m_use - m_cand);
+              m_use = m_cand;
+            }
+            rescale_o_cols<D>(tO, alpha);
+            nm2 = f2_pack(-m_use, -m_use);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(C::B_P_FULL + t));
+#pragma unroll
+          for (int c = P_SPLIT; c < 4; ++c) {
+            uint32_t pk[16];
+            make_p32_sum<BF16, emu_pair_mask<D>()>(s[c], sc2, nm2, pk, acc2);
+            tmem_st16(tP + c * 16, pk);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(bar(C::B_P_LATE + t));
+          const uint64_t acc01 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
+          float sl0, sl1;
+          f2_unpack(acc01, sl0, sl1);
+          l = l * alpha + (sl0 + sl1);
+          continue;
+        }
         if (masked) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) mask_chunk(s[c], c * 32, lim);
