@@ -12,8 +12,7 @@ Every variant computes the full attention (no work is skipped); they differ only
   p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
   no_spec_max    the row max taken before any exp2 (FA2_SPEC_MAX=0) instead of in parallel with
                  the first chunks, with a redo when a max moves
-  qk_split       QK issued as two N=64 halves, the first before PV has read P (FA2_QK_SPLIT=1),
-                 instead of one N=128 GEMM after PV
+  two_issuers    one MMA-issuing thread per Q tile (FA2_TWO_ISSUERS=1) instead of one for both
   pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
                  packs whenever the group divides 128; the reference's rule would not pack here)
   pack_off_headline, pack_off_mqa   the same on the headline and on an MQA shape
@@ -46,8 +45,8 @@ COMPILED = {
     "emu_25": ["-DFA2_EMU_MASK_D128=0x2222u", "-DFA2_EMU_MASK_D64=0x2222u"],
     "emu_50": ["-DFA2_EMU_MASK_D128=0x5555u", "-DFA2_EMU_MASK_D64=0x5555u"],
     "p_split_2": ["-DFA2_P_SPLIT=2"],
-    "qk_split": ["-DFA2_QK_SPLIT=1"],
     "no_spec_max": ["-DFA2_SPEC_MAX=0"],
+    "two_issuers": ["-DFA2_TWO_ISSUERS=1"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

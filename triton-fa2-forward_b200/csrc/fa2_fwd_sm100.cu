@@ -22,7 +22,7 @@
 //   warps 4-7   softmax for Q tile 1
 //   warp  8     tcgen05 MMA issue (one thread) + TMEM allocation
 //   warp  9     TMA producer (one thread)
-//   warps 10-11 idle
+//   warps 10-11 idle (with FA2_TWO_ISSUERS=1, warp 10 issues Q tile 1's MMAs)
 // Registers: launched at 168/thread; setmaxnreg moves them to the softmax warpgroups
 // (200 each) from the MMA/TMA warpgroup (104): 2 * 200 + 104 == 3 * 168.
 // TMEM (512 columns x 128 lanes, fp32):  S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [..+D)
@@ -61,6 +61,7 @@ constexpr int NUM_WARPS = 12;
 constexpr int NUM_THREADS = NUM_WARPS * 32;
 constexpr int SOFTMAX_WARPS = 8;
 constexpr int MMA_WARP = 8;
+constexpr int MMA_WARP2 = 10;  // second MMA issuer (Q tile 1) with FA2_TWO_ISSUERS
 constexpr int LOAD_WARP = 9;
 constexpr int TMEM_COLS = 512;
 constexpr int REGS_SOFTMAX = 200;
@@ -89,12 +90,12 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // first tile) redoes its P before the hand-off. Same values as taking the max first.
 #define FA2_SPEC_MAX 1
 #endif
-#ifndef FA2_QK_SPLIT
-// 1: each QK GEMM is issued as two N = 64 halves. The half writing S columns 0-63 does not
-// touch P (columns 64-127), so it is issued right after the first part of the previous PV.
-// Measured 22% slower at the headline (the second operand read twice, N = 64 MMAs, and the low
-// half queued ahead of the rest of PV); kept as an ablation alternative.
-#define FA2_QK_SPLIT 0
+#ifndef FA2_TWO_ISSUERS
+// 1: (no split-KV pairs) warp 8 issues Q tile 0's MMAs and warp 10 tile 1's, so one tile's
+// hand-offs are not served after the other tile's MMA issue. 0 (shipped): warp 8 issues both,
+// whole GEMMs in the order PV(0) QK(0) PV(1) QK(1). Measured: two issuers 16-19% slower on every
+// config (the tensor pipe then interleaves the two tiles' MMAs); kept as an ablation alternative.
+#define FA2_TWO_ISSUERS 0
 #endif
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
@@ -361,6 +362,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (!get_unit<CAUSAL>(a, 0, u0) || u0.J <= 0) return;  // nothing to do (uniform, before any sync)
   }
 
+  // MMA-issuing threads: every K/V slot is released, and the teardown barrier arrived at, by each.
+  const uint32_t issuers = (FA2_TWO_ISSUERS && !dual) ? 2u : 1u;
   if (warp == LOAD_WARP && lane == 0) {
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(C::B_Q + t), 1);
@@ -372,9 +375,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(C::B_KV_FULL + s), 1);
-      mbar_init(bar(C::B_KV_EMPTY + s), 1);
+      mbar_init(bar(C::B_KV_EMPTY + s), issuers);
     }
-    mbar_init(bar(C::B_MMA_DONE), 1);
+    mbar_init(bar(C::B_MMA_DONE), issuers);
     fence_mbar_init();
     fence_proxy_async_smem();
   }
@@ -482,10 +485,11 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       if (q_loads0 > 0) mbar_wait(bar(C::B_Q + 0), static_cast<uint32_t>(q_loads0 - 1) & 1u, DEFAULT_TIMEOUT, nullptr);
       if (q_loads1 > 0) mbar_wait(bar(C::B_Q + 1), static_cast<uint32_t>(q_loads1 - 1) & 1u, DEFAULT_TIMEOUT, nullptr);
     }
-  } else if (warp == MMA_WARP) {
+  } else if (warp == MMA_WARP || warp == MMA_WARP2) {
     reg_dealloc<REGS_OTHER>();
-    // -------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // -------------------------------------------------------------- MMA issuer(s)
+    const bool second = (warp == MMA_WARP2);  // issues Q tile 1's MMAs with two issuers
+    if (lane == 0 && (!second || issuers == 2)) {
       constexpr uint32_t idesc_qk = idesc_f16(BF16, BM, BN, false);
       constexpr uint32_t idesc_pv = idesc_f16(BF16, BM, D, true);
       // Descriptors of the tile bases; a byte offset o inside shared memory adds o >> 4 to
@@ -501,18 +505,6 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint64_t off = static_cast<uint64_t>(((kk >> 2) * C::CHUNK_BYTES + (kk & 3) * 32) >> 4);
           mma_ss(tmem + t * BN, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
-        }
-      };
-      // QK of tile t, score columns [64 h, 64 h + 64) only: K rows 64 h .. 64 h + 63, which sit
-      // 8 KiB into each 16 KiB swizzle chunk of the K tile.
-      constexpr uint32_t idesc_qk64 = idesc_f16(BF16, BM, BN / 2, false);
-      auto issue_qk_half = [&](int t, int st, int h) {
-        const uint64_t qd = dq_base + static_cast<uint64_t>((t * C::TILE_BYTES) >> 4);
-        const uint64_t kd = dk_base + static_cast<uint64_t>((st * C::TILE_BYTES + h * (BN / 2) * 128) >> 4);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint64_t off = static_cast<uint64_t>(((kk >> 2) * C::CHUNK_BYTES + (kk & 3) * 32) >> 4);
-          mma_ss(tmem + t * BN + h * (BN / 2), qd + off, kd + off, idesc_qk64, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int t, int st, bool acc, int kk0, int kk1) {
@@ -585,6 +577,48 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             if (!ok) break;
           }
         } while (false);
+      } else if (issuers == 2) {
+        // One Q tile per issuing thread. Each walks the same units and ring entries, releases
+        // every K/V slot once (the slot barrier expects both) and commits its tile's barriers.
+        const int t = second ? 1 : 0;
+        do {
+          if (!mwait(C::B_Q + t, 0) || !kv_wait(0)) { ok = false; break; }
+          tc_fence_after();
+          issue_qk(t, 0);
+          mma_commit(bar(C::B_S_FULL + t));
+          mma_commit(bar(C::B_KV_EMPTY + 0));
+          if (u.J == 1) mma_commit(bar(C::B_Q_EMPTY + t));
+          int n = 0, i = 0, g = 0;  // unit, ring position of its K_0, steps of the units before
+          while (true) {
+            Unit nx;
+            const bool has_next = get_unit<CAUSAL>(a, n + 1, nx);
+            const uint32_t qph_next = static_cast<uint32_t>(n + 1) & 1u;
+            for (int j = 0; j < u.J; ++j) {
+              const bool last = (j + 1 == u.J);
+              const int iv = i + 2 * j + 1, ik = i + 2 * j + 2;  // V_j, then K_j+1 (or the next unit's K_0)
+              const int sv = iv % C::STAGES, sk = ik % C::STAGES;
+              const bool more = !last || has_next;
+              const bool qk_final = last ? (has_next && nx.J == 1) : (j + 2 == u.J);
+              const uint32_t pph = static_cast<uint32_t>(g + j) & 1u;
+              if (!kv_wait(iv) || !pv_tile(t, sv, j > 0, pph)) { ok = false; break; }
+              mma_commit(bar(C::B_KV_EMPTY + sv));
+              if (last) mma_commit(bar(C::B_O_FULL + t));
+              if (more) {
+                if ((last && !mwait(C::B_Q + t, qph_next)) || !kv_wait(ik)) { ok = false; break; }
+                tc_fence_after();
+                issue_qk(t, sk);
+                mma_commit(bar(C::B_S_FULL + t));
+                mma_commit(bar(C::B_KV_EMPTY + sk));
+                if (qk_final) mma_commit(bar(C::B_Q_EMPTY + t));
+              }
+            }
+            if (!ok || !has_next) break;
+            i += 2 * u.J;
+            g += u.J;
+            ++n;
+            u = nx;
+          }
+        } while (false);
       } else {
         do {
           // First unit: QK of both tiles on its K_0. Later units' first QKs are issued in the
@@ -614,33 +648,6 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
               // The QK issued below is its unit's last one for tile t: Q_t may be reloaded after it.
               const bool qk_final = last ? (has_next && nx.J == 1) : (j + 2 == u.J);
               const uint32_t pph = static_cast<uint32_t>(g + j) & 1u;
-#if FA2_QK_SPLIT
-              // Per tile: PV part 1, QK low half (S columns 0-63; the softmax has read S, as its
-              // P_FULL arrival shows), PV part 2, QK high half (after PV has read P).
-              if (!kv_wait(iv)) { ok = false; break; }
-              for (int t = 0; t < 2; ++t) {
-                if (!mwait(C::B_P_FULL + t, pph)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv(t, sv, j > 0, 0, 2 * P_SPLIT);
-                if (more) {
-                  if ((last && !mwait(C::B_Q + t, qph_next)) || (t == 0 && !kv_wait(ik))) { ok = false; break; }
-                  tc_fence_after();
-                  issue_qk_half(t, sk, 0);
-                }
-                if (!mwait(C::B_P_LATE + t, pph)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv(t, sv, j > 0, 2 * P_SPLIT, BN / 16);
-                if (t == 1) mma_commit(bar(C::B_KV_EMPTY + sv));
-                if (last) mma_commit(bar(C::B_O_FULL + t));
-                if (more) {
-                  issue_qk_half(t, sk, 1);
-                  mma_commit(bar(C::B_S_FULL + t));
-                  if (t == 1) mma_commit(bar(C::B_KV_EMPTY + sk));
-                  if (qk_final) mma_commit(bar(C::B_Q_EMPTY + t));
-                }
-              }
-              if (!ok) break;
-#else
               if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
               if (last) mma_commit(bar(C::B_O_FULL + 0));
               if (more) {
@@ -661,7 +668,6 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 mma_commit(bar(C::B_KV_EMPTY + sk));
                 if (qk_final) mma_commit(bar(C::B_Q_EMPTY + 1));
               }
-#endif
             }
             if (!ok || !has_next) break;
             i += 2 * u.J;
@@ -902,7 +908,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     }
     if (lane == 0) bulk_wait_all();  // the last stores have read the slot and written O
   } else {
-    reg_dealloc<REGS_OTHER>();  // warps 10-11: nothing to do
+    reg_dealloc<REGS_OTHER>();  // warp 11 (and warp 10 with one issuer): nothing to do
   }
 
   if (!ok && a.err != nullptr) atomicOr(a.err, FA2_ERR_TIMEOUT);
