@@ -90,6 +90,14 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // first tile) redoes its P before the hand-off. Same values as taking the max first.
 #define FA2_SPEC_MAX 1
 #endif
+#ifndef FA2_STAGES_D128
+// K/V ring slots of 32 KiB at D = 128. 4 fit beside Q and the O staging, but 3 measured ~1%
+// faster (headline and MHA causal, two boxes); 2 is 3% slower.
+#define FA2_STAGES_D128 3
+#endif
+#ifndef FA2_STAGES_D64
+#define FA2_STAGES_D64 8   // K/V ring slots of 16 KiB at D = 64
+#endif
 #ifndef FA2_TWO_ISSUERS
 // 1: (no split-KV pairs) warp 8 issues Q tile 0's MMAs and warp 10 tile 1's, so one tile's
 // hand-offs are not served after the other tile's MMA issue. 0 (shipped): warp 8 issues both,
@@ -115,7 +123,8 @@ struct Cfg {
   static constexpr int CHUNKS = D / 64;             // 64-element (128-byte) swizzle atoms along d
   static constexpr int CHUNK_BYTES = 128 * 128;     // 128 rows x 128 bytes
   static constexpr int TILE_BYTES = BN * D * 2;     // == BM * D * 2
-  static constexpr int STAGES = (D == 128) ? 4 : 8; // K/V ring depth (K_j and V_j take one slot each)
+  // K/V ring depth (K_j and V_j take one slot each)
+  static constexpr int STAGES = (D == 128) ? FA2_STAGES_D128 : FA2_STAGES_D64;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = Q_TILES * TILE_BYTES;
   // O staging for the TMA store: one slot of 32 rows x 64 columns (128-byte swizzle, the
