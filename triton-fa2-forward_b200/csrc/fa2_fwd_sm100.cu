@@ -98,6 +98,13 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_STAGES_D64
 #define FA2_STAGES_D64 8   // K/V ring slots of 16 KiB at D = 64
 #endif
+#ifndef FA2_STG_FULL
+// 1: each softmax warp stages all of its 32 O rows (every 64-column chunk) before one set of
+// TMA stores, so no chunk waits for the previous chunk's store to read the slot (+1.5..2% on
+// the short-unit pack_tail config, neutral elsewhere). 0: one 64-column chunk slot per warp,
+// reused chunk by chunk.
+#define FA2_STG_FULL 1
+#endif
 #ifndef FA2_TWO_ISSUERS
 // 1: (no split-KV pairs) warp 8 issues Q tile 0's MMAs and warp 10 tile 1's, so one tile's
 // hand-offs are not served after the other tile's MMA issue. 0 (shipped): warp 8 issues both,
@@ -129,9 +136,10 @@ struct Cfg {
   static constexpr int OFF_KV = Q_TILES * TILE_BYTES;
   // O staging for the TMA store: one slot of 32 rows x 64 columns (128-byte swizzle, the
   // O tensor map's box) per softmax warp.
-  static constexpr int STG_SLOT_BYTES = 32 * 128;
+  static constexpr int STG_SLOT_BYTES = 32 * 128;                        // one 64-column chunk
+  static constexpr int STG_WARP_BYTES = (FA2_STG_FULL ? CHUNKS : 1) * STG_SLOT_BYTES;
   static constexpr int OFF_STG = OFF_KV + STAGES * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_STG + SOFTMAX_WARPS * STG_SLOT_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + SOFTMAX_WARPS * STG_WARP_BYTES;
   // barrier slots
   static constexpr int B_Q = 0;                     // [2]  Q tile landed
   static constexpr int B_KV_FULL = 2;               // [S]  K/V tile landed
@@ -702,7 +710,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t tO = tmem + lane_addr + C::TMEM_O + t * D;
     const float qk_scale = a.qk_scale;
     const uint64_t sc2 = f2_pack(qk_scale, qk_scale);
-    const uint32_t so = sbase + C::OFF_STG + warp * C::STG_SLOT_BYTES;  // this warp's O staging slot
+    const uint32_t so = sbase + C::OFF_STG + warp * C::STG_WARP_BYTES;  // this warp's O staging slot
 
     int g = 0;  // steps of the units before
     Unit u;
@@ -898,18 +906,26 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                       x0, x1);
             pk[e] = cvt_pack2<BF16>(x0, x1);
           }
-          if (lane == 0) bulk_wait_read();
-          __syncwarp();
+          const uint32_t slot = so + (FA2_STG_FULL ? ch * C::STG_SLOT_BYTES : 0);
+          if (!FA2_STG_FULL || ch == 0) {
+            if (lane == 0) bulk_wait_read();  // the slot's previous stores have read it
+            __syncwarp();
+          }
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
-            st_shared_v4(so + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
+            st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
                          pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
           }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0 && pos0 < a.n_q) {
-            tma_store_4d(&tmO, so, ch * 64, h0, pos0, u.b);
-            bulk_commit();
+          if (!FA2_STG_FULL || ch == C::CHUNKS - 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && pos0 < a.n_q) {
+#pragma unroll
+              for (int c2 = (FA2_STG_FULL ? 0 : ch); c2 <= ch; ++c2) {
+                tma_store_4d(&tmO, so + (FA2_STG_FULL ? c2 * C::STG_SLOT_BYTES : 0), c2 * 64, h0, pos0, u.b);
+              }
+              bulk_commit();
+            }
           }
         }
       }
