@@ -13,7 +13,8 @@ Every variant computes the full attention (no work is skipped); they differ only
   no_spec_max    the row max taken before any exp2 (FA2_SPEC_MAX=0) instead of in parallel with
                  the first chunks, with a redo when a max moves
   two_issuers    one MMA-issuing thread per Q tile (FA2_TWO_ISSUERS=1) instead of one for both
-  stages_4, stages_2   K/V ring of 4 (2) slots at D=128, 8 (4) at D=64 (shipped: 3 and 8)
+  stages_4, stages_2   K/V ring of 4 (2) slots at D=128, 8 (4) at D=64 (shipped: 3 and 8); the
+                 4-slot ring only fits with one O staging chunk per warp
   stg_chunk      O staged one 64-column chunk at a time per warp (FA2_STG_FULL=0) instead of whole
   pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
                  packs whenever the group divides 128; the reference's rule would not pack here)
@@ -49,7 +50,7 @@ COMPILED = {
     "p_split_2": ["-DFA2_P_SPLIT=2"],
     "no_spec_max": ["-DFA2_SPEC_MAX=0"],
     "two_issuers": ["-DFA2_TWO_ISSUERS=1"],
-    "stages_4": ["-DFA2_STAGES_D128=4", "-DFA2_STAGES_D64=8"],
+    "stages_4": ["-DFA2_STAGES_D128=4", "-DFA2_STAGES_D64=8", "-DFA2_STG_FULL=0"],
     "stages_2": ["-DFA2_STAGES_D128=2", "-DFA2_STAGES_D64=4"],
     "stg_chunk": ["-DFA2_STG_FULL=0"],
 }

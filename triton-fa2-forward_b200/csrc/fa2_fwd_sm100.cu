@@ -124,20 +124,22 @@ static_assert(P_SPLIT >= 1 && P_SPLIT <= 3, "P hand-off split");
 // setmaxnreg draws on the registers the CTA was launched with (384 threads x 168).
 static_assert(2 * REGS_SOFTMAX + REGS_OTHER <= 3 * 168, "register split exceeds the launch budget");
 
-template <int D>
+// Shared-memory layout of one CTA. SPLIT: the split-KV build, which writes fp32 partials from
+// registers (no O staging) and, streaming K/V from HBM, uses a deeper ring.
+template <int D, bool SPLIT = false>
 struct Cfg {
   static_assert(D == 64 || D == 128, "compiled head dims");
   static constexpr int CHUNKS = D / 64;             // 64-element (128-byte) swizzle atoms along d
   static constexpr int CHUNK_BYTES = 128 * 128;     // 128 rows x 128 bytes
   static constexpr int TILE_BYTES = BN * D * 2;     // == BM * D * 2
   // K/V ring depth (K_j and V_j take one slot each)
-  static constexpr int STAGES = (D == 128) ? FA2_STAGES_D128 : FA2_STAGES_D64;
+  static constexpr int STAGES = SPLIT ? ((D == 128) ? 4 : 8) : ((D == 128) ? FA2_STAGES_D128 : FA2_STAGES_D64);
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = Q_TILES * TILE_BYTES;
   // O staging for the TMA store: one slot of 32 rows x 64 columns (128-byte swizzle, the
   // O tensor map's box) per softmax warp.
   static constexpr int STG_SLOT_BYTES = 32 * 128;                        // one 64-column chunk
-  static constexpr int STG_WARP_BYTES = (FA2_STG_FULL ? CHUNKS : 1) * STG_SLOT_BYTES;
+  static constexpr int STG_WARP_BYTES = SPLIT ? 0 : (FA2_STG_FULL ? CHUNKS : 1) * STG_SLOT_BYTES;
   static constexpr int OFF_STG = OFF_KV + STAGES * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_STG + SOFTMAX_WARPS * STG_WARP_BYTES;
   // barrier slots
@@ -358,12 +360,13 @@ __device__ __forceinline__ void rescale_o_cols(uint32_t tO, float alpha) {
 }
 
 // ------------------------------------------------------------------------ kernel
-template <int D, bool CAUSAL, bool BF16>
+// SPLIT: the split-KV build (num_splits > 1); the host launches it exactly then.
+template <int D, bool CAUSAL, bool BF16, bool SPLIT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
                const KArgs a) {
-  using C = Cfg<D>;
+  using C = Cfg<D, SPLIT>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t sraw = smem_u32(smem_raw);
   const uint32_t sbase = (sraw + 1023u) & ~1023u;
@@ -858,7 +861,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       }
       tc_fence_after();
-      if (a.num_splits > 1) {
+      if constexpr (SPLIT) {
         // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
         // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
         const bool has = (l > 0.0f);
@@ -1083,15 +1086,16 @@ SplitPlan plan_splits(const Fa2FwdParams* p) {
 
 template <int D, bool CAUSAL, bool BF16>
 int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
-  using C = Cfg<D>;
-  auto kern = fa2::fa2_fwd_kernel<D, CAUSAL, BF16>;
-  static bool attr_done[kMaxDevices] = {};
+  const bool split = plan_splits(p).num_splits > 1;
+  auto kern = split ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, true> : fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false>;
+  const int smem_alloc = split ? Cfg<D, true>::SMEM_ALLOC : Cfg<D, false>::SMEM_ALLOC;
+  static bool attr_done[2][kMaxDevices] = {};
   if (device < 0 || device >= kMaxDevices) return FA2_ERR_DEVICE;
-  if (!attr_done[device]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_ALLOC) != cudaSuccess) {
+  if (!attr_done[split][device]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_alloc) != cudaSuccess) {
       return FA2_ERR_LAUNCH;
     }
-    attr_done[device] = true;
+    attr_done[split][device] = true;
   }
   const int group = p->heads_q / p->heads_kv;
   const int pack = p->pack_gqa ? group : 1;
@@ -1160,7 +1164,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
     if (sms <= 0) return FA2_ERR_DEVICE;
     grid = dim3(static_cast<unsigned>(units < sms ? units : sms), 1, 1);  // one CTA per SM
   }
-  kern<<<grid, fa2::NUM_THREADS, C::SMEM_ALLOC, stream>>>(tmQ, tmK, tmV, tmO, ka);
+  kern<<<grid, fa2::NUM_THREADS, smem_alloc, stream>>>(tmQ, tmK, tmV, tmO, ka);
   if (cudaGetLastError() != cudaSuccess) return FA2_ERR_LAUNCH;
   if (sp.num_splits > 1) {
     fa2::CombineArgs ca;
