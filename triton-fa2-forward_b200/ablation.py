@@ -6,9 +6,15 @@ Every variant computes the full attention (no work is skipped); they differ only
   shipped        the library as built by build.py
   no_persistent  one CTA per 256-row work unit (FA2_PERSISTENT=0) instead of one CTA per SM
                  walking the units
-  all_mufu       every exp2 on the MUFU (shipped: 25% on the FMA pipe at D=128, none at D=64)
-  emu_25         25% of the exp2 on the FMA pipe at both head dims
+  all_mufu       every exp2 on the MUFU (shipped: 25% on the FMA pipe at D=128; at D=64 12.5%
+                 for bf16 and none for fp16)
+  emu_25         25% of the exp2 (pairs 3, 7, 11, 15) on the FMA pipe at both head dims
   emu_50         half of the exp2 on the FMA pipe at both head dims
+  emu_25_pairs_0/1/2   25% at D=128 on pairs 0,4,8,12 / 1,5,9,13 / 2,6,10,14 of each chunk
+                 (shipped: 3, 7, 11, 15)
+  emu_d64_12     12.5% (pairs 7, 15) on the FMA pipe at D=64 for fp16 too (shipped: bf16 only)
+  d64_bf16_all_mufu   every exp2 on the MUFU at D=64 bf16
+  emu_12, emu_12_pairs_7, emu_37   12.5% (pairs 1,9 / 7,15) or 37.5% on the FMA pipe at D=128
   p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
   no_spec_max    the row max taken before any exp2 (FA2_SPEC_MAX=0) instead of in parallel with
                  the first chunks, with a redo when a max moves
@@ -44,9 +50,17 @@ BUILD_DIR = os.path.join(PKG_DIR, "_build", "ablation")
 COMPILED = {
     "shipped": [],
     "no_persistent": ["-DFA2_PERSISTENT=0"],
-    "all_mufu": ["-DFA2_EMU_MASK_D128=0x0u", "-DFA2_EMU_MASK_D64=0x0u"],
-    "emu_25": ["-DFA2_EMU_MASK_D128=0x2222u", "-DFA2_EMU_MASK_D64=0x2222u"],
-    "emu_50": ["-DFA2_EMU_MASK_D128=0x5555u", "-DFA2_EMU_MASK_D64=0x5555u"],
+    "all_mufu": ["-DFA2_EMU_MASK_D128=0x0u", "-DFA2_EMU_MASK_D64=0x0u", "-DFA2_EMU_MASK_D64_BF16=0x0u"],
+    "emu_25": ["-DFA2_EMU_MASK_D128=0x8888u", "-DFA2_EMU_MASK_D64=0x8888u", "-DFA2_EMU_MASK_D64_BF16=0x8888u"],
+    "emu_50": ["-DFA2_EMU_MASK_D128=0x5555u", "-DFA2_EMU_MASK_D64=0x5555u", "-DFA2_EMU_MASK_D64_BF16=0x5555u"],
+    "emu_25_pairs_0": ["-DFA2_EMU_MASK_D128=0x1111u"],
+    "emu_25_pairs_1": ["-DFA2_EMU_MASK_D128=0x2222u"],
+    "emu_25_pairs_2": ["-DFA2_EMU_MASK_D128=0x4444u"],
+    "emu_12": ["-DFA2_EMU_MASK_D128=0x0202u"],
+    "emu_12_pairs_7": ["-DFA2_EMU_MASK_D128=0x8080u"],
+    "emu_d64_12": ["-DFA2_EMU_MASK_D64=0x8080u"],
+    "d64_bf16_all_mufu": ["-DFA2_EMU_MASK_D64_BF16=0x0u"],
+    "emu_37": ["-DFA2_EMU_MASK_D128=0x2A2Au"],
     "p_split_2": ["-DFA2_P_SPLIT=2"],
     "no_spec_max": ["-DFA2_SPEC_MAX=0"],
     "two_issuers": ["-DFA2_TWO_ISSUERS=1"],

@@ -69,14 +69,18 @@ constexpr int REGS_OTHER = 104;
 constexpr float RESCALE_TH = 8.0f;               // log2 units: P may reach 2^8 before a rescale
 constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // Which of the 16 exp2 pairs of a 32-column chunk run on the FMA pipe (the rest on the MUFU).
-// D = 128: pairs 1, 5, 9, 13, i.e. 25% on the FMA pipe. D = 64: none. Each has half the
-// tensor work per score and less pipe headroom for the polynomial; measured all-MUFU
-// +0.6..3.5% at D = 64, -1..2% at D = 128.
+// D = 128: pairs 3, 7, 11, 15, i.e. 25% on the FMA pipe (the same share on pairs 1, 5, 9, 13
+// measured 1.4% slower on two boxes; 37.5% is 6% slower). D = 64 has half the tensor work per
+// score and less pipe headroom for the polynomial: bf16 (degree-3 polynomial) puts pairs 7 and
+// 15 on the FMA pipe (12.5%, +2..5% over all-MUFU), fp16 (degree 4) runs every exp2 on the MUFU.
 #ifndef FA2_EMU_MASK_D128
-#define FA2_EMU_MASK_D128 0x2222u
+#define FA2_EMU_MASK_D128 0x8888u
 #endif
 #ifndef FA2_EMU_MASK_D64
 #define FA2_EMU_MASK_D64 0x0u
+#endif
+#ifndef FA2_EMU_MASK_D64_BF16
+#define FA2_EMU_MASK_D64_BF16 0x8080u
 #endif
 #ifndef FA2_P_SPLIT
 #define FA2_P_SPLIT 3  // P chunks (of 32 columns) handed to the MMA warp before the rest
@@ -115,9 +119,10 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
 #endif
-template <int D>
+template <int D, bool BF16>
 __host__ __device__ constexpr uint32_t emu_pair_mask() {
-  return D == 128 ? static_cast<uint32_t>(FA2_EMU_MASK_D128) : static_cast<uint32_t>(FA2_EMU_MASK_D64);
+  return D == 128 ? static_cast<uint32_t>(FA2_EMU_MASK_D128)
+                  : (BF16 ? static_cast<uint32_t>(FA2_EMU_MASK_D64_BF16) : static_cast<uint32_t>(FA2_EMU_MASK_D64));
 }
 constexpr int P_SPLIT = FA2_P_SPLIT;
 static_assert(P_SPLIT >= 1 && P_SPLIT <= 3, "P hand-off split");
@@ -762,7 +767,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
             for (int c = 0; c < P_SPLIT; ++c) {
               uint32_t pk[16];
-              make_p32_sum<BF16, emu_pair_mask<D>()>(s[c], sc2, nm2, pk, acc2);
+              make_p32_sum<BF16, emu_pair_mask<D, BF16>()>(s[c], sc2, nm2, pk, acc2);
               tmem_st16(tP + c * 16, pk);
             }
             if (pass == 1) break;
@@ -781,7 +786,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
           for (int c = P_SPLIT; c < 4; ++c) {
             uint32_t pk[16];
-            make_p32_sum<BF16, emu_pair_mask<D>()>(s[c], sc2, nm2, pk, acc2);
+            make_p32_sum<BF16, emu_pair_mask<D, BF16>()>(s[c], sc2, nm2, pk, acc2);
             tmem_st16(tP + c * 16, pk);
           }
           tmem_wait_st();
@@ -821,7 +826,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           if (masked) {
             make_p32<BF16, 0u>(s[c], sc2, nm2, pk);
           } else {
-            make_p32<BF16, emu_pair_mask<D>()>(s[c], sc2, nm2, pk);
+            make_p32<BF16, emu_pair_mask<D, BF16>()>(s[c], sc2, nm2, pk);
           }
           tmem_st16(tP + c * 16, pk);
           if (c == P_SPLIT - 1) {
