@@ -22,6 +22,7 @@ Every variant computes the full attention (no work is skipped); they differ only
   stages_4, stages_2   K/V ring of 4 (2) slots at D=128, 8 (4) at D=64 (shipped: 3 and 8); the
                  4-slot ring only fits with one O staging chunk per warp
   stg_chunk      O staged one 64-column chunk at a time per warp (FA2_STG_FULL=0) instead of whole
+  no_l2_hints    TMA loads with evict_normal in L2 (FA2_L2_HINTS=0) instead of K/V evict_last, Q evict_first
   pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
                  packs whenever the group divides 128; the reference's rule would not pack here)
   pack_off_headline, pack_off_mqa   the same on the headline and on an MQA shape
@@ -67,6 +68,7 @@ COMPILED = {
     "stages_4": ["-DFA2_STAGES_D128=4", "-DFA2_STAGES_D64=8", "-DFA2_STG_FULL=0"],
     "stages_2": ["-DFA2_STAGES_D128=2", "-DFA2_STAGES_D64=4"],
     "stg_chunk": ["-DFA2_STG_FULL=0"],
+    "no_l2_hints": ["-DFA2_L2_HINTS=0"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

@@ -109,6 +109,9 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // reused chunk by chunk.
 #define FA2_STG_FULL 1
 #endif
+#ifndef FA2_L2_HINTS
+#define FA2_L2_HINTS 1  // 1: K/V loads evict_last, Q loads evict_first in L2; 0: evict_normal for both
+#endif
 #ifndef FA2_TWO_ISSUERS
 // 1: (no split-KV pairs) warp 8 issues Q tile 0's MMAs and warp 10 tile 1's, so one tile's
 // hand-offs are not served after the other tile's MMA issue. 0 (shipped): warp 8 issues both,
@@ -426,8 +429,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       tma_prefetch_desc(&tmO);
-      const uint64_t pol_kv = l2_policy_evict_last();   // K/V are re-read by every Q block
-      const uint64_t pol_q = l2_policy_evict_first();   // Q is read once
+      // K/V are re-read by every Q block of their head, Q is read once.
+      const uint64_t pol_kv = FA2_L2_HINTS ? l2_policy_evict_last() : l2_policy_evict_normal();
+      const uint64_t pol_q = FA2_L2_HINTS ? l2_policy_evict_first() : l2_policy_evict_normal();
       int q_loads0 = 0, q_loads1 = 0;
       auto load_q = [&](const Unit& u, int t) {
         const int R = u.row0 + t * BM;
