@@ -23,6 +23,8 @@ Every variant computes the full attention (no work is skipped); they differ only
                  4-slot ring only fits with one O staging chunk per warp
   stg_chunk      O staged one 64-column chunk at a time per warp (FA2_STG_FULL=0) instead of whole
   no_l2_hints    TMA loads with evict_normal in L2 (FA2_L2_HINTS=0) instead of K/V evict_last, Q evict_first
+  mma_spin       the MMA thread polls its barriers without suspending (FA2_MMA_SPIN=1)
+  rescale_th_12  the running max moves only past 2^12 (FA2_RESCALE_TH=12) instead of 2^8
   pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
                  packs whenever the group divides 128; the reference's rule would not pack here)
   pack_off_headline, pack_off_mqa   the same on the headline and on an MQA shape
@@ -69,6 +71,8 @@ COMPILED = {
     "stages_2": ["-DFA2_STAGES_D128=2", "-DFA2_STAGES_D64=4"],
     "stg_chunk": ["-DFA2_STG_FULL=0"],
     "no_l2_hints": ["-DFA2_L2_HINTS=0"],
+    "mma_spin": ["-DFA2_MMA_SPIN=1"],
+    "rescale_th_12": ["-DFA2_RESCALE_TH=12.0f"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

@@ -66,7 +66,10 @@ constexpr int LOAD_WARP = 9;
 constexpr int TMEM_COLS = 512;
 constexpr int REGS_SOFTMAX = 200;
 constexpr int REGS_OTHER = 104;
-constexpr float RESCALE_TH = 8.0f;               // log2 units: P may reach 2^8 before a rescale
+#ifndef FA2_RESCALE_TH
+#define FA2_RESCALE_TH 8.0f
+#endif
+constexpr float RESCALE_TH = FA2_RESCALE_TH;     // log2 units: P may reach 2^8 before a rescale
 constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // Which of the 16 exp2 pairs of a 32-column chunk run on the FMA pipe (the rest on the MUFU).
 // D = 128: pairs 3, 7, 11, 15, i.e. 25% on the FMA pipe (the same share on pairs 1, 5, 9, 13
