@@ -98,8 +98,8 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #define FA2_SPEC_MAX 1
 #endif
 #ifndef FA2_STAGES_D128
-// K/V ring slots of 32 KiB at D = 128. 4 fit beside Q and the O staging, but 3 measured ~1%
-// faster (headline and MHA causal, two boxes); 2 is 3% slower.
+// K/V ring slots of 32 KiB at D = 128 (the split-KV build uses 4). A 4th slot fits only with
+// one O staging chunk per warp and measured 1-2% slower (headline, three boxes); 2 is 3% slower.
 #define FA2_STAGES_D128 3
 #endif
 #ifndef FA2_STAGES_D64
