@@ -73,7 +73,7 @@ int main(void) {
   CHECK(fa2_fwd_sm100_check(&p) == FA2_ERR_WORKSPACE, "split-KV without a workspace is rejected");
 
   int32_t bm = 0, bn = 0, th = 0, st = 0, sm = 0;
-  CHECK(fa2_fwd_sm100_config(128, &bm, &bn, &th, &st, &sm) == FA2_OK && bm == 128 && bn == 128 && th == 384 &&
+  CHECK(fa2_fwd_sm100_config(128, &bm, &bn, &th, &st, &sm) == FA2_OK && bm == 128 && bn == 128 && (th == 384 || th == 640) &&
             st >= 2 && sm > 0 && sm <= 227 * 1024,
         "config of the D=128 kernel");
   CHECK(fa2_fwd_sm100_config(80, &bm, &bn, &th, &st, &sm) == FA2_ERR_HEAD_DIM, "config rejects D=80");

@@ -41,7 +41,7 @@ def test_config_entry_point():
     with pytest.raises(_lib.Fa2Error):
         _lib.config(96)
     bm, bn, warps, stages = _default_config(128, True)
-    assert (bm, bn) == (128, 128) and warps == 12 and stages >= 2
+    assert (bm, bn) == (128, 128) and warps in (12, 20) and stages >= 2  # 8 or 16 softmax warps
     assert _default_config(64, False)[0] == 128
 
 

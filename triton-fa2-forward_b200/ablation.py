@@ -25,6 +25,9 @@ Every variant computes the full attention (no work is skipped); they differ only
   no_l2_hints    TMA loads with evict_normal in L2 (FA2_L2_HINTS=0) instead of K/V evict_last, Q evict_first
   mma_spin       the MMA thread polls its barriers without suspending (FA2_MMA_SPIN=1)
   rescale_th_12  the running max moves only past 2^12 (FA2_RESCALE_TH=12) instead of 2^8
+  row_split_2    two softmax warps per row quadrant, 64 scores each, exchanging the row max and
+                 row sum through TMEM (FA2_ROW_SPLIT=2: 20 warps, setmaxnreg 104/64) instead of
+                 one warp taking all 128 scores (12 warps, 200/104)
   pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
                  packs whenever the group divides 128; the reference's rule would not pack here)
   pack_off_headline, pack_off_mqa   the same on the headline and on an MQA shape
@@ -73,6 +76,7 @@ COMPILED = {
     "no_l2_hints": ["-DFA2_L2_HINTS=0"],
     "mma_spin": ["-DFA2_MMA_SPIN=1"],
     "rescale_th_12": ["-DFA2_RESCALE_TH=12.0f"],
+    "row_split_2": ["-DFA2_ROW_SPLIT=2"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

@@ -25,6 +25,8 @@
 //   warps 10-11 idle (with FA2_TWO_ISSUERS=1, warp 10 issues Q tile 1's MMAs)
 // Registers: launched at 168/thread; setmaxnreg moves them to the softmax warpgroups
 // (200 each) from the MMA/TMA warpgroup (104): 2 * 200 + 104 == 3 * 168.
+// (FA2_ROW_SPLIT=2, a measured-slower alternative: 640 threads, two softmax warps per lane
+// quadrant with 64 scores each, warps 16-19 MMA / TMA / spare.)
 // TMEM (512 columns x 128 lanes, fp32):  S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [..+D)
 //   P_t (fp16/bf16, packed 2 per column) overwrites the upper half of S_t, and the second
 //   GEMM reads it straight from TMEM (tcgen05.mma A-from-TMEM).
@@ -57,15 +59,33 @@ namespace fa2 {
 constexpr int BM = 128;  // rows per Q tile (one TMEM lane each)
 constexpr int BN = 128;  // K/V rows per tile
 constexpr int Q_TILES = 2;
-constexpr int NUM_WARPS = 12;
+#ifndef FA2_ROW_SPLIT
+// Softmax warps per TMEM lane quadrant of a Q tile. 1: one warp takes all 128 scores of its
+// 32 rows (12 warps: 8 softmax, MMA, TMA, 2 spare). 2: two warps take 64 scores each and
+// exchange the row max and row sum through TMEM (20 warps: 16 softmax, MMA, TMA, 2 spare).
+#define FA2_ROW_SPLIT 1
+#endif
+#ifndef FA2_RS2_REGS_SOFTMAX
+#define FA2_RS2_REGS_SOFTMAX 104  // with FA2_ROW_SPLIT=2; the other warpgroup gets what is left (64)
+#endif
+constexpr int HALVES = FA2_ROW_SPLIT;
+static_assert(HALVES == 1 || HALVES == 2, "row split");
+constexpr int SCOLS = BN / HALVES;  // scores of a row per softmax warp
+constexpr int SOFTMAX_WARPS = 8 * HALVES;
+constexpr int MMA_WARP = SOFTMAX_WARPS;
+constexpr int LOAD_WARP = SOFTMAX_WARPS + 1;
+constexpr int MMA_WARP2 = SOFTMAX_WARPS + 2;  // second MMA issuer (Q tile 1) with FA2_TWO_ISSUERS
+constexpr int NUM_WARPS = HALVES == 1 ? 12 : 20;  // whole warpgroups (setmaxnreg works on warpgroups)
 constexpr int NUM_THREADS = NUM_WARPS * 32;
-constexpr int SOFTMAX_WARPS = 8;
-constexpr int MMA_WARP = 8;
-constexpr int MMA_WARP2 = 10;  // second MMA issuer (Q tile 1) with FA2_TWO_ISSUERS
-constexpr int LOAD_WARP = 9;
 constexpr int TMEM_COLS = 512;
-constexpr int REGS_SOFTMAX = 200;
-constexpr int REGS_OTHER = 104;
+// Launched at REGS_LAUNCH registers a thread (the launch bound's share: 65536 / 384 -> 168,
+// and with 20 warps five per SMSP, 16384 / 160 -> 96); setmaxnreg then moves registers from
+// the MMA/TMA warpgroup to the softmax warpgroups. The new counts must fit in what the CTA
+// was launched with.
+constexpr int REGS_LAUNCH = HALVES == 1 ? 168 : 96;
+constexpr int REGS_SOFTMAX = HALVES == 1 ? 200 : FA2_RS2_REGS_SOFTMAX;
+constexpr int REGS_OTHER =
+    HALVES == 1 ? 104 : (((NUM_WARPS * REGS_LAUNCH - SOFTMAX_WARPS * REGS_SOFTMAX) / (NUM_WARPS - SOFTMAX_WARPS)) & ~7);
 #ifndef FA2_RESCALE_TH
 #define FA2_RESCALE_TH 8.0f
 #endif
@@ -132,8 +152,18 @@ __host__ __device__ constexpr uint32_t emu_pair_mask() {
 }
 constexpr int P_SPLIT = FA2_P_SPLIT;
 static_assert(P_SPLIT >= 1 && P_SPLIT <= 3, "P hand-off split");
-// setmaxnreg draws on the registers the CTA was launched with (384 threads x 168).
-static_assert(2 * REGS_SOFTMAX + REGS_OTHER <= 3 * 168, "register split exceeds the launch budget");
+constexpr int NCH = SCOLS / 32;                          // 32-score chunks per softmax warp
+constexpr int P_SPLIT_W = HALVES == 1 ? P_SPLIT : 1;     // of them, handed over before the rest
+// TMEM columns of S_t, per warp: its SCOLS scores at t * BN + h * SCOLS. P (2 per column)
+// overwrites the upper half of that range; with HALVES == 2 the lowest column, read into
+// registers like the rest, then carries the warp's row max to the other warp of the row.
+constexpr int P_OFF = SCOLS / 2;
+// setmaxnreg draws on the registers the CTA was launched with (threads x REGS_LAUNCH).
+static_assert(SOFTMAX_WARPS * REGS_SOFTMAX + (NUM_WARPS - SOFTMAX_WARPS) * REGS_OTHER <= NUM_WARPS * REGS_LAUNCH,
+              "register split exceeds the launch budget");
+static_assert(REGS_OTHER >= 24 && REGS_SOFTMAX % 8 == 0 && REGS_OTHER % 8 == 0, "setmaxnreg counts");
+static_assert(NUM_THREADS * REGS_LAUNCH <= 65536, "launch register budget");
+static_assert(HALVES == 1 || !FA2_TWO_ISSUERS, "two MMA issuers need the 12-warp layout");
 
 // Shared-memory layout of one CTA. SPLIT: the split-KV build, which writes fp32 partials from
 // registers (no O staging) and, streaming K/V from HBM, uses a deeper ring.
@@ -147,12 +177,17 @@ struct Cfg {
   static constexpr int STAGES = SPLIT ? ((D == 128) ? 4 : 8) : ((D == 128) ? FA2_STAGES_D128 : FA2_STAGES_D64);
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = Q_TILES * TILE_BYTES;
-  // O staging for the TMA store: one slot of 32 rows x 64 columns (128-byte swizzle, the
-  // O tensor map's box) per softmax warp.
+  // Epilogue: each epilogue warp writes EPI_COLS columns of O for its 32 rows. With two
+  // warps per row, D = 128 gives each 64 columns; at D = 64 the first warp of the row
+  // writes all of them.
+  static constexpr int EPI_COLS = (HALVES == 2 && D == 128) ? 64 : D;
+  static constexpr int EPI_WARPS = (EPI_COLS * HALVES == D) ? SOFTMAX_WARPS : 8;
+  // O staging for the TMA store: slots of 32 rows x 64 columns (128-byte swizzle, the
+  // O tensor map's box) per epilogue warp.
   static constexpr int STG_SLOT_BYTES = 32 * 128;                        // one 64-column chunk
-  static constexpr int STG_WARP_BYTES = SPLIT ? 0 : (FA2_STG_FULL ? CHUNKS : 1) * STG_SLOT_BYTES;
+  static constexpr int STG_WARP_BYTES = SPLIT ? 0 : (FA2_STG_FULL ? EPI_COLS / 64 : 1) * STG_SLOT_BYTES;
   static constexpr int OFF_STG = OFF_KV + STAGES * TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_STG + SOFTMAX_WARPS * STG_WARP_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + EPI_WARPS * STG_WARP_BYTES;
   // barrier slots
   static constexpr int B_Q = 0;                     // [2]  Q tile landed
   static constexpr int B_KV_FULL = 2;               // [S]  K/V tile landed
@@ -163,12 +198,19 @@ struct Cfg {
   static constexpr int B_MMA_DONE = 8 + 2 * STAGES; // [1]  every MMA retired (teardown)
   static constexpr int B_P_LATE = 9 + 2 * STAGES;   // [2]  the remaining P_t columns in TMEM
   static constexpr int B_Q_EMPTY = 11 + 2 * STAGES; // [2]  last QK of tile t of a unit retired: Q_t reloadable
-  static constexpr int NUM_BARS = 13 + 2 * STAGES;
+  static constexpr int B_XCH = 13 + 2 * STAGES;     // [8]  (HALVES == 2) row-pair exchange of tile t, quadrant q
+  static constexpr int NUM_BARS = 13 + 2 * STAGES + (HALVES == 2 ? 8 : 0);
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
   static constexpr int TMEM_O = 2 * BN;                 // O_t at TMEM_O + t * D
   static_assert(TMEM_O + 2 * D <= TMEM_COLS, "TMEM budget");
+  // HALVES == 2: column that carries warp h's row sum to the other warp of the row in the
+  // epilogue. D = 128: the first of its own O columns (read before it is overwritten);
+  // D = 64: spare columns past O_1.
+  __device__ static constexpr int tmem_lx(int t, int h) {
+    return D == 128 ? TMEM_O + t * D + h * 64 : TMEM_O + 2 * D + t * 2 + h;
+  }
   static_assert(SMEM_ALLOC <= 227 * 1024, "shared memory budget");
 };
 
@@ -297,6 +339,17 @@ __device__ __forceinline__ float row_max64(const uint32_t (&s0)[32], const uint3
   return fmax3(fmaxf(m0, m1), m2, m3);
 }
 
+// Max of a warp's scores of its row: 128 (four chunks) or 64 (two).
+template <int N>
+__device__ __forceinline__ float row_max_chunks(const uint32_t (&s)[N][32]) {
+  static_assert(N == 2 || N == 4, "chunks per softmax warp");
+  if constexpr (N == 4) {
+    return fmaxf(row_max64(s[0], s[1]), row_max64(s[2], s[3]));
+  } else {
+    return row_max64(s[0], s[1]);
+  }
+}
+
 // Scores of columns c0 + i with c0 + i > lim are set to -inf (causal / end-of-sequence mask).
 __device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], int c0, int lim) {
 #pragma unroll
@@ -400,9 +453,12 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       mbar_init(bar(C::B_Q + t), 1);
       mbar_init(bar(C::B_Q_EMPTY + t), 1);
       mbar_init(bar(C::B_S_FULL + t), 1);
-      mbar_init(bar(C::B_P_FULL + t), BM);
-      mbar_init(bar(C::B_P_LATE + t), BM);
+      mbar_init(bar(C::B_P_FULL + t), BM * HALVES);
+      mbar_init(bar(C::B_P_LATE + t), BM * HALVES);
       mbar_init(bar(C::B_O_FULL + t), 1);
+    }
+    if constexpr (HALVES == 2) {
+      for (int x = 0; x < 8; ++x) mbar_init(bar(C::B_XCH + x), 64);
     }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(C::B_KV_FULL + s), 1);
@@ -517,7 +573,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       if (q_loads0 > 0) mbar_wait(bar(C::B_Q + 0), static_cast<uint32_t>(q_loads0 - 1) & 1u, DEFAULT_TIMEOUT, nullptr);
       if (q_loads1 > 0) mbar_wait(bar(C::B_Q + 1), static_cast<uint32_t>(q_loads1 - 1) & 1u, DEFAULT_TIMEOUT, nullptr);
     }
-  } else if (warp == MMA_WARP || warp == MMA_WARP2) {
+  } else if (warp == MMA_WARP || (HALVES == 1 && warp == MMA_WARP2)) {
     reg_dealloc<REGS_OTHER>();
     // -------------------------------------------------------------- MMA issuer(s)
     const bool second = (warp == MMA_WARP2);  // issues Q tile 1's MMAs with two issuers
@@ -539,27 +595,33 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           mma_ss(tmem + t * BN, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
+      // k-steps [kk0, kk1) of each softmax warp's SCOLS scores: 16 scores each, P packed
+      // 2 per TMEM column at t * BN + h * SCOLS + P_OFF, V rows h * SCOLS + 16 * kk.
       auto issue_pv = [&](int t, int st, bool acc, int kk0, int kk1) {
         const uint64_t vd = dv_base + static_cast<uint64_t>((st * C::TILE_BYTES) >> 4);
 #pragma unroll
-        for (int kk = kk0; kk < kk1; ++kk) {
-          mma_ts(tmem + C::TMEM_O + t * D, tmem + t * BN + BN / 2 + kk * 8,
-                 vd + static_cast<uint64_t>((kk * 16 * 128) >> 4), idesc_pv, (acc || kk > 0) ? 1u : 0u);
+        for (int h = 0; h < HALVES; ++h) {
+#pragma unroll
+          for (int kk = kk0; kk < kk1; ++kk) {
+            const int k0 = h * SCOLS + kk * 16;  // first score (V row) of this k-step
+            mma_ts(tmem + C::TMEM_O + t * D, tmem + t * BN + h * SCOLS + P_OFF + kk * 8,
+                   vd + static_cast<uint64_t>((k0 * 128) >> 4), idesc_pv, (acc || k0 > 0) ? 1u : 0u);
+          }
         }
       };
       auto mwait = [&](int b_idx, uint32_t parity) -> bool {
         return FA2_MMA_SPIN ? mbar_wait_spin(bar(b_idx), parity, a.timeout, a.err)
                             : mbar_wait(bar(b_idx), parity, a.timeout, a.err);
       };
-      // PV of tile t in two parts: the k-steps reading P columns [0, 32 * P_SPLIT), which
-      // the softmax warps hand over before computing the rest, then the remaining k-steps.
+      // PV of tile t in two parts: the k-steps reading each softmax warp's first P_SPLIT_W
+      // 32-score chunks, which the warps hand over before computing the rest, then the others.
       auto pv_tile = [&](int t, int st, bool acc, uint32_t pph) -> bool {
         if (!mwait(C::B_P_FULL + t, pph)) return false;
         tc_fence_after();
-        issue_pv(t, st, acc, 0, 2 * P_SPLIT);
+        issue_pv(t, st, acc, 0, 2 * P_SPLIT_W);
         if (!mwait(C::B_P_LATE + t, pph)) return false;
         tc_fence_after();
-        issue_pv(t, st, acc, 2 * P_SPLIT, BN / 16);
+        issue_pv(t, st, acc, 2 * P_SPLIT_W, SCOLS / 16);
         return true;
       };
       auto kv_wait = [&](int i) -> bool {
@@ -716,16 +778,43 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   } else if (warp < SOFTMAX_WARPS) {
     reg_alloc<REGS_SOFTMAX>();
     // ------------------------------------------------------------------ softmax
-    const int t = warp >> 2;          // Q tile
-    const int q = warp & 3;           // TMEM lane quadrant of this warp
+    // warp = t * 4 * HALVES + h * 4 + q: Q tile t, TMEM lane quadrant q (the lanes of the
+    // warp's SMSP) and, with HALVES == 2, which SCOLS scores h of each row.
+    const int q = warp & 3;
+    const int h = (warp >> 2) & (HALVES - 1);
+    const int t = warp / (4 * HALVES);
     const int r = q * 32 + lane;      // row within the tile == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-    const uint32_t tS = tmem + lane_addr + t * BN;
-    const uint32_t tP = tS + BN / 2;
+    const uint32_t tS = tmem + lane_addr + t * BN + h * SCOLS;            // this warp's scores
+    [[maybe_unused]] const uint32_t tS_other = tmem + lane_addr + t * BN + (h ^ 1) * SCOLS;  // the other warp's (HALVES == 2)
+    const uint32_t tP = tS + P_OFF;
     const uint32_t tO = tmem + lane_addr + C::TMEM_O + t * D;
     const float qk_scale = a.qk_scale;
     const uint64_t sc2 = f2_pack(qk_scale, qk_scale);
-    const uint32_t so = sbase + C::OFF_STG + warp * C::STG_WARP_BYTES;  // this warp's O staging slot
+    constexpr int RCOLS = D / HALVES;  // O columns this warp rescales
+    constexpr bool ALL_EPI = (C::EPI_WARPS == SOFTMAX_WARPS);
+    const bool epi = ALL_EPI || h == 0;             // this warp writes O columns [epi_c0, + EPI_COLS)
+    const int epi_c0 = ALL_EPI ? h * C::EPI_COLS : 0;
+    const uint32_t so = sbase + C::OFF_STG + (ALL_EPI ? warp : t * 4 + q) * C::STG_WARP_BYTES;  // O staging
+
+    // HALVES == 2: the two warps of a row pair (same t and q) each publish one value per row in
+    // a TMEM column and read the other's once both have arrived on the pair's barrier. One
+    // exchange per K/V step (the row max) and one per unit (the row sum), so the parity is a
+    // running count; the wait is bounded like every other.
+    uint32_t xph = 0;
+    auto exchange = [&](uint32_t col_mine, uint32_t col_other, float v, float& other) -> bool {
+      tmem_st1(col_mine, __float_as_uint(v));
+      tmem_wait_st();
+      tc_fence_before();
+      const uint32_t xb = bar(C::B_XCH + t * 4 + q);
+      mbar_arrive(xb);
+      const bool w = mbar_wait(xb, xph, a.timeout, a.err);
+      xph ^= 1u;
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      other = __uint_as_float(tmem_ld1_wait(col_other));
+      return true;
+    };
 
     int g = 0;  // steps of the units before
     Unit u;
@@ -737,8 +826,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       const int pos = (tile_row0 + r) >> a.pack_shift;      // sequence position of this row
       const int tile_pos0 = tile_row0 >> a.pack_shift;      // position of the tile's first row
 
-      float m_use = -INFINITY;  // reference max of this row (scaled, base 2)
-      float l = 0.0f;
+      float m_use = -INFINITY;  // reference max of this row (scaled, base 2), the same in both warps of a pair
+      float l = 0.0f;           // row sum over this warp's scores
       for (int j = 0; j < J; ++j) {
         bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(g + j) & 1u, a.timeout, a.err);
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
@@ -746,52 +835,58 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         const int col0 = (kv_base + j) * BN;
         const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
         const bool need_pad = (col0 + BN > a.n_kv);
-        const bool masked = need_causal || need_pad;  // uniform over the warpgroup
+        const bool masked = need_causal || need_pad;  // uniform over the tile's warps
         int lim = a.n_kv - 1 - col0;                  // last visible column of this tile, relative
         if (CAUSAL) lim = min(lim, pos - col0);
 
-        // The whole S row (128 columns) in one batch of loads and a single wait.
-        uint32_t s[4][32];
+        // This warp's scores of the row in one batch of loads and a single wait.
+        uint32_t s[NCH][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, s[c]);
+        for (int c = 0; c < NCH; ++c) tmem_ld32(tS + c * 32, s[c]);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) reg_fence32(s[c]);
+        for (int c = 0; c < NCH; ++c) reg_fence32(s[c]);
         if (FA2_SPEC_MAX && !masked && j > 0 && __all_sync(0xffffffffu, m_use != -INFINITY)) {
           // P with the current reference max while the row max is taken (the two are independent
           // and use different pipes); the threshold test then runs before the hand-off.
-          const float m_cand = fmaxf(row_max64(s[0], s[1]), row_max64(s[2], s[3])) * qk_scale;
+          float m_cand = row_max_chunks(s) * qk_scale;
           uint64_t nm2 = f2_pack(-m_use, -m_use);
           uint64_t acc2[4];
           float alpha = 1.0f;
           // Pass 0 uses the current reference max. If some row's max moved past the threshold
-          // (rare), pass 1 moves it, rescales O_t (PV(t, j-1) has retired: S_t(j) was committed
-          // after it) and redoes these chunks with the new reference max.
+          // (rare), pass 1 moves it, rescales this warp's O_t columns (PV(t, j-1) has retired:
+          // S_t(j) was committed after it) and redoes these chunks with the new reference max.
 #pragma unroll 1
           for (int pass = 0;; ++pass) {
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc2[i] = 0;
 #pragma unroll
-            for (int c = 0; c < P_SPLIT; ++c) {
+            for (int c = 0; c < P_SPLIT_W; ++c) {
               uint32_t pk[16];
               make_p32_sum<BF16, emu_pair_mask<D, BF16>()>(s[c], sc2, nm2, pk, acc2);
               tmem_st16(tP + c * 16, pk);
             }
             if (pass == 1) break;
+            if constexpr (HALVES == 2) {
+              float m_other;
+              if (!exchange(tS, tS_other, m_cand, m_other)) { ok = false; break; }
+              m_cand = fmaxf(m_cand, m_other);
+            }
             const bool bump = m_cand > m_use + RESCALE_TH;
             if (!__any_sync(0xffffffffu, bump)) break;
             if (bump) {
               alpha = ex2_mufu(m_use - m_cand);
               m_use = m_cand;
             }
-            rescale_o_cols<D>(tO, alpha);
+            rescale_o_cols<RCOLS>(tO + h * RCOLS, alpha);
             nm2 = f2_pack(-m_use, -m_use);
           }
+          if (!ok) break;
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(bar(C::B_P_FULL + t));
 #pragma unroll
-          for (int c = P_SPLIT; c < 4; ++c) {
+          for (int c = P_SPLIT_W; c < NCH; ++c) {
             uint32_t pk[16];
             make_p32_sum<BF16, emu_pair_mask<D, BF16>()>(s[c], sc2, nm2, pk, acc2);
             tmem_st16(tP + c * 16, pk);
@@ -807,9 +902,14 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         }
         if (masked) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) mask_chunk(s[c], c * 32, lim);
+          for (int c = 0; c < NCH; ++c) mask_chunk(s[c], h * SCOLS + c * 32, lim);
         }
-        const float m_cand = fmaxf(row_max64(s[0], s[1]), row_max64(s[2], s[3])) * qk_scale;
+        float m_cand = row_max_chunks(s) * qk_scale;
+        if constexpr (HALVES == 2) {
+          float m_other;
+          if (!exchange(tS, tS_other, m_cand, m_other)) { ok = false; break; }
+          m_cand = fmaxf(m_cand, m_other);
+        }
         const bool bump = m_cand > m_use + RESCALE_TH;  // first tile: always (m_use = -inf)
         float alpha = 1.0f;
         if (bump) {
@@ -818,17 +918,17 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         }
         if (j > 0 && __any_sync(0xffffffffu, bump)) {
           // PV(t, j-1) has retired: S_t(j) was committed after it.
-          rescale_o_cols<D>(tO, alpha);
+          rescale_o_cols<RCOLS>(tO + h * RCOLS, alpha);
         }
 
-        // P = exp2(s * qk_scale - m) into TMEM; the first P_SPLIT chunks are handed to the
+        // P = exp2(s * qk_scale - m) into TMEM; the first P_SPLIT_W chunks are handed to the
         // MMA warp before the rest are computed, so PV can start on them.
         // A row that has seen only masked columns so far (possible inside a split) keeps
         // m_use = -inf; its p must be exactly 0, not exp2(-inf + inf).
         const float m_safe = (m_use == -INFINITY) ? 0.0f : m_use;
         const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < NCH; ++c) {
           uint32_t pk[16];
           if (masked) {
             make_p32<BF16, 0u>(s[c], sc2, nm2, pk);
@@ -836,7 +936,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             make_p32<BF16, emu_pair_mask<D, BF16>()>(s[c], sc2, nm2, pk);
           }
           tmem_st16(tP + c * 16, pk);
-          if (c == P_SPLIT - 1) {
+          if (c == P_SPLIT_W - 1) {
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::B_P_FULL + t));
@@ -849,7 +949,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         // Row sum of the fp32 p (before rounding, as fa2/kernel.py:98), off the critical path.
         uint64_t acc2[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < NCH; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             acc2[(i >> 1) & 3] =
@@ -873,73 +973,92 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
       }
       tc_fence_after();
-      if constexpr (SPLIT) {
-        // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
-        // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
-        const bool has = (l > 0.0f);
-        const float inv_l = has ? 1.0f / l : 0.0f;
-        const int split_idx = dual ? 2 * static_cast<int>(blockIdx.z) + t : static_cast<int>(blockIdx.z);
-        const int64_t slot = (static_cast<int64_t>(split_idx) * gridDim.x + u.x) * a.rows_pad + tile_row0 + r;
-        float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D);
+      constexpr int EC = C::EPI_COLS / 32;  // 32-column chunks of O this warp writes
+      uint32_t o[EC][32];
+      auto load_o = [&]() {
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld();
-          reg_fence32(o);
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            dst[c * 8 + v] = make_float4(__uint_as_float(o[4 * v]) * inv_l, __uint_as_float(o[4 * v + 1]) * inv_l,
-                                         __uint_as_float(o[4 * v + 2]) * inv_l, __uint_as_float(o[4 * v + 3]) * inv_l);
-          }
-        }
-        a.lse_part[slot] = has ? m_use + log2f(l) : -INFINITY;
-      } else {
-        // O / l in the input dtype, 64 columns at a time through this warp's staging slot and
-        // one TMA store per chunk. Lane 0 issued every store from the slot, so it alone waits
-        // for the slot to have been read before it is rewritten (the next chunk's conversion
-        // overlaps the read).
-        uint32_t o[D / 32][32];
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) tmem_ld32(tO + c * 32, o[c]);
+        for (int c = 0; c < EC; ++c) tmem_ld32(tO + epi_c0 + c * 32, o[c]);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) reg_fence32(o[c]);
-        const float inv_l = 1.0f / l;
-        const uint64_t inv2 = f2_pack(inv_l, inv_l);
-        const int R0 = tile_row0 + q * 32;  // first row of this warp
-        const int pos0 = R0 >> a.pack_shift;
-        const int h0 = u.hq0 + (R0 & (a.pack - 1));
+        for (int c = 0; c < EC; ++c) reg_fence32(o[c]);
+      };
+      // Every warp writes O (ALL_EPI): its O columns are read before the row-sum exchange, whose
+      // column at D = 128 is the first of them. Otherwise (D = 64, two warps a row) the writing
+      // warp reads them after it, where it uses them.
+      if constexpr (ALL_EPI) load_o();
+      float l_row = l;
+      if constexpr (HALVES == 2) {
+        // The row sum is the two partial sums, the first warp's first in both warps.
+        float l_other;
+        if (!exchange(tmem + lane_addr + C::tmem_lx(t, h), tmem + lane_addr + C::tmem_lx(t, h ^ 1), l, l_other)) {
+          ok = false;
+          break;
+        }
+        l_row = (h == 0) ? l + l_other : l_other + l;
+      }
+      if (epi) {
+        if constexpr (!ALL_EPI) load_o();
+        if constexpr (SPLIT) {
+          // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
+          // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
+          const bool has = (l_row > 0.0f);
+          const float inv_l = has ? 1.0f / l_row : 0.0f;
+          const int split_idx = dual ? 2 * static_cast<int>(blockIdx.z) + t : static_cast<int>(blockIdx.z);
+          const int64_t slot = (static_cast<int64_t>(split_idx) * gridDim.x + u.x) * a.rows_pad + tile_row0 + r;
+          float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D + epi_c0);
 #pragma unroll
-        for (int ch = 0; ch < C::CHUNKS; ++ch) {
-          uint32_t pk[32];
+          for (int c = 0; c < EC; ++c) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const uint32_t* src = o[2 * ch + (e >> 4)];
-            float x0, x1;
-            f2_unpack(f2_mul(f2_pack(__uint_as_float(src[(2 * e) & 31]), __uint_as_float(src[(2 * e + 1) & 31])), inv2),
-                      x0, x1);
-            pk[e] = cvt_pack2<BF16>(x0, x1);
+            for (int v = 0; v < 8; ++v) {
+              dst[c * 8 + v] = make_float4(__uint_as_float(o[c][4 * v]) * inv_l, __uint_as_float(o[c][4 * v + 1]) * inv_l,
+                                           __uint_as_float(o[c][4 * v + 2]) * inv_l, __uint_as_float(o[c][4 * v + 3]) * inv_l);
+            }
           }
-          const uint32_t slot = so + (FA2_STG_FULL ? ch * C::STG_SLOT_BYTES : 0);
-          if (!FA2_STG_FULL || ch == 0) {
-            if (lane == 0) bulk_wait_read();  // the slot's previous stores have read it
-            __syncwarp();
-          }
+          if (h == 0) a.lse_part[slot] = has ? m_use + log2f(l_row) : -INFINITY;
+        } else {
+          // O / l in the input dtype, 64 columns at a time through this warp's staging slot and
+          // one TMA store per chunk. Lane 0 issued every store from the slot, so it alone waits
+          // for the slot to have been read before it is rewritten (the next chunk's conversion
+          // overlaps the read).
+          constexpr int ECH = C::EPI_COLS / 64;  // 64-column chunks
+          const float inv_l = 1.0f / l_row;
+          const uint64_t inv2 = f2_pack(inv_l, inv_l);
+          const int R0 = tile_row0 + q * 32;  // first row of this warp
+          const int pos0 = R0 >> a.pack_shift;
+          const int h0 = u.hq0 + (R0 & (a.pack - 1));
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
-                         pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
-          }
-          if (!FA2_STG_FULL || ch == C::CHUNKS - 1) {
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0 && pos0 < a.n_q) {
+          for (int ch = 0; ch < ECH; ++ch) {
+            const uint32_t slot = so + (FA2_STG_FULL ? ch * C::STG_SLOT_BYTES : 0);
+            if (!FA2_STG_FULL || ch == 0) {
+              if (lane == 0) bulk_wait_read();  // the slot's previous stores have read it
+              __syncwarp();
+            }
 #pragma unroll
-              for (int c2 = (FA2_STG_FULL ? 0 : ch); c2 <= ch; ++c2) {
-                tma_store_4d(&tmO, so + (FA2_STG_FULL ? c2 * C::STG_SLOT_BYTES : 0), c2 * 64, h0, pos0, u.b);
+            for (int v = 0; v < 8; ++v) {
+              // columns ch * 64 + 8 v .. + 8 of this warp's share, as four packed pairs
+              const uint32_t* src = o[2 * ch + (v >> 2)];
+              uint32_t w4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int e = (v & 3) * 8 + 2 * i;
+                float x0, x1;
+                f2_unpack(f2_mul(f2_pack(__uint_as_float(src[e]), __uint_as_float(src[e + 1])), inv2), x0, x1);
+                w4[i] = cvt_pack2<BF16>(x0, x1);
               }
-              bulk_commit();
+              st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
+                           w4[0], w4[1], w4[2], w4[3]);
+            }
+            if (!FA2_STG_FULL || ch == ECH - 1) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0 && pos0 < a.n_q) {
+#pragma unroll
+                for (int c2 = (FA2_STG_FULL ? 0 : ch); c2 <= ch; ++c2) {
+                  tma_store_4d(&tmO, so + (FA2_STG_FULL ? c2 * C::STG_SLOT_BYTES : 0), epi_c0 + c2 * 64, h0, pos0,
+                               u.b);
+                }
+                bulk_commit();
+              }
             }
           }
         }
@@ -948,7 +1067,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     }
     if (lane == 0) bulk_wait_all();  // the last stores have read the slot and written O
   } else {
-    reg_dealloc<REGS_OTHER>();  // warp 11 (and warp 10 with one issuer): nothing to do
+    // The spare warps of the MMA/TMA warpgroup (warp 10 also issues with two issuers).
+    reg_dealloc<REGS_OTHER>();
   }
 
   if (!ok && a.err != nullptr) atomicOr(a.err, FA2_ERR_TIMEOUT);

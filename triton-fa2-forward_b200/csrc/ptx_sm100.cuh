@@ -280,6 +280,22 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// One 32-bit column of this warp's 32 lanes: store, and load followed by its wait (one asm
+// statement, so no use of the value can be scheduled above the wait).
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t tmem_ld1_wait(uint32_t taddr) {
+  uint32_t v;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(v)
+      : "r"(taddr)
+      : "memory");
+  return v;
+}
+
 // tcgen05.ld writes its destination registers asynchronously; they are valid only after
 // tcgen05.wait::ld. This empty asm "redefines" the registers after the wait so the
 // compiler cannot schedule any use of them above it.
