@@ -25,6 +25,11 @@ Every variant computes the full attention (no work is skipped); they differ only
   no_l2_hints    TMA loads with evict_normal in L2 (FA2_L2_HINTS=0) instead of K/V evict_last, Q evict_first
   mma_spin       the MMA thread polls its barriers without suspending (FA2_MMA_SPIN=1)
   rescale_th_12  the running max moves only past 2^12 (FA2_RESCALE_TH=12) instead of 2^8
+  regs_208       softmax warps at 208 registers, the MMA/TMA warpgroup at 88 (shipped: 200 / 104)
+  s_load_x64     a softmax warp's scores loaded from TMEM in 64-column tcgen05.ld instructions
+                 (shipped: four of 32 columns at D=128, one of 128 at D=64)
+  d128_s_load_x128, d64_s_load_x32   the other load width at one head dim
+  d64_regs_208   208 / 88 registers at D=64 only
   row_split_2    two softmax warps per row quadrant, 64 scores each, exchanging the row max and
                  row sum through TMEM (FA2_ROW_SPLIT=2: 20 warps, setmaxnreg 104/64) instead of
                  one warp taking all 128 scores (12 warps, 200/104)
@@ -77,6 +82,11 @@ COMPILED = {
     "mma_spin": ["-DFA2_MMA_SPIN=1"],
     "rescale_th_12": ["-DFA2_RESCALE_TH=12.0f"],
     "row_split_2": ["-DFA2_ROW_SPLIT=2"],
+    "regs_208": ["-DFA2_REGS_SOFTMAX_D128=208", "-DFA2_REGS_SOFTMAX_D64=208"],
+    "s_load_x64": ["-DFA2_S_LOAD_X_D128=64", "-DFA2_S_LOAD_X_D64=64"],
+    "d128_s_load_x128": ["-DFA2_S_LOAD_X_D128=128"],
+    "d64_s_load_x32": ["-DFA2_S_LOAD_X_D64=32"],
+    "d64_regs_208": ["-DFA2_REGS_SOFTMAX_D64=208"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

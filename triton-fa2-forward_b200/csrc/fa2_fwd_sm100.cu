@@ -82,10 +82,36 @@ constexpr int TMEM_COLS = 512;
 // and with 20 warps five per SMSP, 16384 / 160 -> 96); setmaxnreg then moves registers from
 // the MMA/TMA warpgroup to the softmax warpgroups. The new counts must fit in what the CTA
 // was launched with.
+// Softmax warps' registers in the 12-warp layout, per head dim (the MMA/TMA warpgroup gets
+// 504 - 2x). Measured: 208 at D = 128 leaves the MMA thread spilling, -6.5%.
+#ifndef FA2_REGS_SOFTMAX_D128
+#define FA2_REGS_SOFTMAX_D128 200
+#endif
+#ifndef FA2_REGS_SOFTMAX_D64
+#define FA2_REGS_SOFTMAX_D64 200
+#endif
+// Columns per tcgen05.ld when a softmax warp loads its scores (32, 64 or 128), per head dim.
+// Measured: one 128-column load is +3% at D = 64 fp16 (bf16 unchanged) and -0.2% at D = 128;
+// 64-column loads are -4% at D = 128.
+#ifndef FA2_S_LOAD_X_D128
+#define FA2_S_LOAD_X_D128 32
+#endif
+#ifndef FA2_S_LOAD_X_D64
+#define FA2_S_LOAD_X_D64 128
+#endif
 constexpr int REGS_LAUNCH = HALVES == 1 ? 168 : 96;
-constexpr int REGS_SOFTMAX = HALVES == 1 ? 200 : FA2_RS2_REGS_SOFTMAX;
-constexpr int REGS_OTHER =
-    HALVES == 1 ? 104 : (((NUM_WARPS * REGS_LAUNCH - SOFTMAX_WARPS * REGS_SOFTMAX) / (NUM_WARPS - SOFTMAX_WARPS)) & ~7);
+template <int D>
+__host__ __device__ constexpr int regs_softmax() {
+  return HALVES == 2 ? FA2_RS2_REGS_SOFTMAX : (D == 128 ? FA2_REGS_SOFTMAX_D128 : FA2_REGS_SOFTMAX_D64);
+}
+template <int D>
+__host__ __device__ constexpr int regs_other() {
+  return ((NUM_WARPS * REGS_LAUNCH - SOFTMAX_WARPS * regs_softmax<D>()) / (NUM_WARPS - SOFTMAX_WARPS)) & ~7;
+}
+template <int D>
+__host__ __device__ constexpr int s_load_x() {
+  return D == 128 ? FA2_S_LOAD_X_D128 : FA2_S_LOAD_X_D64;
+}
 #ifndef FA2_RESCALE_TH
 #define FA2_RESCALE_TH 8.0f
 #endif
@@ -159,9 +185,12 @@ constexpr int P_SPLIT_W = HALVES == 1 ? P_SPLIT : 1;     // of them, handed over
 // registers like the rest, then carries the warp's row max to the other warp of the row.
 constexpr int P_OFF = SCOLS / 2;
 // setmaxnreg draws on the registers the CTA was launched with (threads x REGS_LAUNCH).
-static_assert(SOFTMAX_WARPS * REGS_SOFTMAX + (NUM_WARPS - SOFTMAX_WARPS) * REGS_OTHER <= NUM_WARPS * REGS_LAUNCH,
-              "register split exceeds the launch budget");
-static_assert(REGS_OTHER >= 24 && REGS_SOFTMAX % 8 == 0 && REGS_OTHER % 8 == 0, "setmaxnreg counts");
+template <int D>
+constexpr bool regs_fit() {
+  return SOFTMAX_WARPS * regs_softmax<D>() + (NUM_WARPS - SOFTMAX_WARPS) * regs_other<D>() <= NUM_WARPS * REGS_LAUNCH &&
+         regs_other<D>() >= 24 && regs_softmax<D>() % 8 == 0 && regs_softmax<D>() <= 256;
+}
+static_assert(regs_fit<128>() && regs_fit<64>(), "register split exceeds the launch budget");
 static_assert(NUM_THREADS * REGS_LAUNCH <= 65536, "launch register budget");
 static_assert(HALVES == 1 || !FA2_TWO_ISSUERS, "two MMA issuers need the 12-warp layout");
 
@@ -481,7 +510,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   bool ok = true;
 
   if (warp == LOAD_WARP) {
-    reg_dealloc<REGS_OTHER>();
+    reg_dealloc<regs_other<D>()>();
     // ------------------------------------------------------------- TMA producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -574,7 +603,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       if (q_loads1 > 0) mbar_wait(bar(C::B_Q + 1), static_cast<uint32_t>(q_loads1 - 1) & 1u, DEFAULT_TIMEOUT, nullptr);
     }
   } else if (warp == MMA_WARP || (HALVES == 1 && warp == MMA_WARP2)) {
-    reg_dealloc<REGS_OTHER>();
+    reg_dealloc<regs_other<D>()>();
     // -------------------------------------------------------------- MMA issuer(s)
     const bool second = (warp == MMA_WARP2);  // issues Q tile 1's MMAs with two issuers
     if (lane == 0 && (!second || issuers == 2)) {
@@ -776,7 +805,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       mbar_wait(bar(C::B_MMA_DONE), 0, DEFAULT_TIMEOUT, nullptr);
     }
   } else if (warp < SOFTMAX_WARPS) {
-    reg_alloc<REGS_SOFTMAX>();
+    reg_alloc<regs_softmax<D>()>();
     // ------------------------------------------------------------------ softmax
     // warp = t * 4 * HALVES + h * 4 + q: Q tile t, TMEM lane quadrant q (the lanes of the
     // warp's SMSP) and, with HALVES == 2, which SCOLS scores h of each row.
@@ -841,8 +870,15 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 
         // This warp's scores of the row in one batch of loads and a single wait.
         uint32_t s[NCH][32];
+        if constexpr (s_load_x<D>() == 128 && NCH == 4) {
+          tmem_ld128(tS, s[0], s[1], s[2], s[3]);
+        } else if constexpr (s_load_x<D>() >= 64) {
 #pragma unroll
-        for (int c = 0; c < NCH; ++c) tmem_ld32(tS + c * 32, s[c]);
+          for (int c = 0; c < NCH; c += 2) tmem_ld64(tS + c * 32, s[c], s[c + 1]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) tmem_ld32(tS + c * 32, s[c]);
+        }
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < NCH; ++c) reg_fence32(s[c]);
@@ -1068,7 +1104,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     if (lane == 0) bulk_wait_all();  // the last stores have read the slot and written O
   } else {
     // The spare warps of the MMA/TMA warpgroup (warp 10 also issues with two issuers).
-    reg_dealloc<REGS_OTHER>();
+    reg_dealloc<regs_other<D>()>();
   }
 
   if (!ok && a.err != nullptr) atomicOr(a.err, FA2_ERR_TIMEOUT);

@@ -263,6 +263,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr));
 }
 
+// 64 or 128 consecutive 32-bit columns in one instruction, into 32-column register chunks.
+#define FA2_RA8(a, i) "=r"(a[i]), "=r"(a[i + 1]), "=r"(a[i + 2]), "=r"(a[i + 3]), "=r"(a[i + 4]), \
+                      "=r"(a[i + 5]), "=r"(a[i + 6]), "=r"(a[i + 7])
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&a0)[32], uint32_t (&a1)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : FA2_RA8(a0, 0), FA2_RA8(a0, 8), FA2_RA8(a0, 16), FA2_RA8(a0, 24), FA2_RA8(a1, 0), FA2_RA8(a1, 8), FA2_RA8(a1, 16), FA2_RA8(a1, 24)
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&a0)[32], uint32_t (&a1)[32], uint32_t (&a2)[32], uint32_t (&a3)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%128];"
+      : FA2_RA8(a0, 0), FA2_RA8(a0, 8), FA2_RA8(a0, 16), FA2_RA8(a0, 24), FA2_RA8(a1, 0), FA2_RA8(a1, 8), FA2_RA8(a1, 16), FA2_RA8(a1, 24), FA2_RA8(a2, 0), FA2_RA8(a2, 8), FA2_RA8(a2, 16), FA2_RA8(a2, 24), FA2_RA8(a3, 0), FA2_RA8(a3, 8), FA2_RA8(a3, 16), FA2_RA8(a3, 24)
+      : "r"(taddr));
+}
+#undef FA2_RA8
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
