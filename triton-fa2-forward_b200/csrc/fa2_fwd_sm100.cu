@@ -91,8 +91,8 @@ constexpr int TMEM_COLS = 512;
 #define FA2_REGS_SOFTMAX_D64 200
 #endif
 // Columns per tcgen05.ld when a softmax warp loads its scores (32, 64 or 128), per head dim.
-// Measured: one 128-column load is +3% at D = 64 fp16 (bf16 unchanged) and -0.2% at D = 128;
-// 64-column loads are -4% at D = 128.
+// Measured: one 128-column load at D = 64 fp16 gave +2.8%, +3.6% and -0.3% on three boxes (bf16
+// unchanged); at D = 128 it is -0.2%, and 64-column loads are -4%.
 #ifndef FA2_S_LOAD_X_D128
 #define FA2_S_LOAD_X_D128 32
 #endif
