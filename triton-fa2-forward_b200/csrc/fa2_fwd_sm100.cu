@@ -78,10 +78,6 @@ constexpr int MMA_WARP2 = SOFTMAX_WARPS + 2;  // second MMA issuer (Q tile 1) wi
 constexpr int NUM_WARPS = HALVES == 1 ? 12 : 20;  // whole warpgroups (setmaxnreg works on warpgroups)
 constexpr int NUM_THREADS = NUM_WARPS * 32;
 constexpr int TMEM_COLS = 512;
-// Launched at REGS_LAUNCH registers a thread (the launch bound's share: 65536 / 384 -> 168,
-// and with 20 warps five per SMSP, 16384 / 160 -> 96); setmaxnreg then moves registers from
-// the MMA/TMA warpgroup to the softmax warpgroups. The new counts must fit in what the CTA
-// was launched with.
 // Softmax warps' registers in the 12-warp layout, per head dim (the MMA/TMA warpgroup gets
 // 504 - 2x). Measured: 208 at D = 128 leaves the MMA thread spilling, -6.5%.
 #ifndef FA2_REGS_SOFTMAX_D128
@@ -99,6 +95,10 @@ constexpr int TMEM_COLS = 512;
 #ifndef FA2_S_LOAD_X_D64
 #define FA2_S_LOAD_X_D64 128
 #endif
+// Launched at REGS_LAUNCH registers a thread (the launch bound's share: 65536 / 384 -> 168,
+// and with 20 warps five per SMSP, 16384 / 160 -> 96); setmaxnreg then moves registers from
+// the MMA/TMA warpgroup to the softmax warpgroups. The new counts must fit in what the CTA
+// was launched with (regs_fit below).
 constexpr int REGS_LAUNCH = HALVES == 1 ? 168 : 96;
 template <int D>
 __host__ __device__ constexpr int regs_softmax() {
