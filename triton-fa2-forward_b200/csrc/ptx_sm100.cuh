@@ -166,21 +166,6 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   return p;
 }
 
-// Named barrier over `count` threads that also ANDs a predicate across them: every
-// participant gets true only if all passed true. Orders shared-memory accesses like bar.sync.
-__device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, %3, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
-      : "memory");
-  return r != 0;
-}
-
 // Warpgroup register re-balancing (all four warps of a warpgroup execute the same one).
 template <int N>
 __device__ __forceinline__ void reg_alloc() {
@@ -281,15 +266,6 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&a0)[32], u
       : "r"(taddr));
 }
 #undef FA2_RA8
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      FA2_S8(0), FA2_S8(8), FA2_S8(16), FA2_S8(24)
-      : "memory");
-}
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
