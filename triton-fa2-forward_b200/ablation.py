@@ -30,6 +30,8 @@ Every variant computes the full attention (no work is skipped); they differ only
                  (shipped: four of 32 columns at D=128, one of 128 at D=64)
   d128_s_load_x128, d64_s_load_x32   the other load width at one head dim
   d64_regs_208   208 / 88 registers at D=64 only
+  fp16_poly_deg3 the degree-3 exp2 polynomial for fp16 P too (shipped: degree 4), with pairs 7 and
+                 15 on the FMA pipe at D=64 fp16 (shipped: none)
   row_split_2    two softmax warps per row quadrant, 64 scores each, exchanging the row max and
                  row sum through TMEM (FA2_ROW_SPLIT=2: 20 warps, setmaxnreg 104/64) instead of
                  one warp taking all 128 scores (12 warps, 200/104)
@@ -87,6 +89,7 @@ COMPILED = {
     "d128_s_load_x128": ["-DFA2_S_LOAD_X_D128=128"],
     "d64_s_load_x32": ["-DFA2_S_LOAD_X_D64=32"],
     "d64_regs_208": ["-DFA2_REGS_SOFTMAX_D64=208"],
+    "fp16_poly_deg3": ["-DFA2_POLY_DEG_FP16=3", "-DFA2_EMU_MASK_D64=0x8080u"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

@@ -122,6 +122,9 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // measured 1.4% slower on two boxes; 37.5% is 6% slower). D = 64 has half the tensor work per
 // score and less pipe headroom for the polynomial: bf16 (degree-3 polynomial) puts pairs 7 and
 // 15 on the FMA pipe (12.5%, +2..5% over all-MUFU), fp16 (degree 4) runs every exp2 on the MUFU.
+#ifndef FA2_POLY_DEG_FP16
+#define FA2_POLY_DEG_FP16 4  // degree of the FMA-pipe exp2 polynomial when P is rounded to fp16
+#endif
 #ifndef FA2_EMU_MASK_D128
 #define FA2_EMU_MASK_D128 0x8888u
 #endif
@@ -398,7 +401,7 @@ __device__ __forceinline__ void make_p32(uint32_t (&s)[32], uint64_t sc2, uint64
     float x0, x1, p0, p1;
     f2_unpack(x2, x0, x1);
     if ((EMU_MASK >> e) & 1u) {
-      exp2_poly_x2<BF16 ? 3 : 4>(x0, x1, p0, p1);
+      exp2_poly_x2<BF16 ? 3 : FA2_POLY_DEG_FP16>(x0, x1, p0, p1);
     } else {
       p0 = ex2_mufu(x0);
       p1 = ex2_mufu(x1);
@@ -420,7 +423,7 @@ __device__ __forceinline__ void make_p32_sum(const uint32_t (&s)[32], uint64_t s
     float x0, x1, p0, p1;
     f2_unpack(x2, x0, x1);
     if ((EMU_MASK >> e) & 1u) {
-      exp2_poly_x2<BF16 ? 3 : 4>(x0, x1, p0, p1);
+      exp2_poly_x2<BF16 ? 3 : FA2_POLY_DEG_FP16>(x0, x1, p0, p1);
     } else {
       p0 = ex2_mufu(x0);
       p1 = ex2_mufu(x1);
