@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define FA2_SM100_ABI_VERSION 2
+#define FA2_SM100_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define FA2_API __attribute__((visibility("default")))
@@ -34,10 +34,18 @@ extern "C" {
 
 enum Fa2DType { FA2_DTYPE_FP16 = 0, FA2_DTYPE_BF16 = 1 };
 
+/* Alignment of the causal mask (Fa2FwdParams::causal_align). Top-left is the reference's
+ * (fa2/kernel.py:225-228): query i sees keys j <= i and N_q must equal N_kv. Bottom-right
+ * lines the last query up with the last key, query i sees keys j <= i + (N_kv - N_q), for
+ * chunked prefill and decode against a longer K/V; it needs N_q <= N_kv (the reference has
+ * no such mode, its README lists it out of scope). With N_q == N_kv the two are the same. */
+enum Fa2CausalAlign { FA2_CAUSAL_TOP_LEFT = 0, FA2_CAUSAL_BOTTOM_RIGHT = 1 };
+
 enum Fa2Status {
   FA2_OK = 0,
   FA2_ERR_NULL = 1,          /* a required pointer is NULL */
-  FA2_ERR_SHAPE = 2,         /* non-positive size, batch mismatch, N_q != N_kv under causal */
+  FA2_ERR_SHAPE = 2,         /* non-positive size, N_q != N_kv under top-left causal, N_q > N_kv
+                                under bottom-right causal, unknown causal_align, num_splits > 256 */
   FA2_ERR_DTYPE = 3,         /* dtype is neither fp16 nor bf16 */
   FA2_ERR_HEAD_DIM = 4,      /* head_dim not supported by the compiled kernels */
   FA2_ERR_GQA = 5,           /* H_q % H_kv != 0 */
@@ -72,7 +80,7 @@ typedef struct Fa2FwdParams {
   int32_t seqlen_kv;
   int32_t head_dim;  /* 64 or 128 */
   int32_t dtype;     /* Fa2DType */
-  int32_t causal;    /* top-left aligned causal mask; requires seqlen_q == seqlen_kv */
+  int32_t causal;    /* causal mask, aligned as causal_align says */
   int32_t pack_gqa;  /* 1: a GQA group's query heads share one 128-row tile */
   float qk_scale;    /* sm_scale * log2(e), > 0 (fa2/kernel.py:240-244) */
   int32_t* err_flag; /* optional device int32; a kernel that gives up on a wait ORs
@@ -86,7 +94,7 @@ typedef struct Fa2FwdParams {
   int32_t num_splits;      /* split-KV: >1 splits every CTA's K/V range into num_splits parts that
                               run as separate CTAs and are merged by a second kernel (short
                               queries against long K/V). <= 1: no split, no workspace. */
-  int32_t reserved0;
+  int32_t causal_align;    /* Fa2CausalAlign; 0 (top-left) is the reference's behaviour */
   void* workspace;         /* device scratch for num_splits > 1 (fp32 partial O + row
                               log-sum-exp), at least fa2_fwd_sm100_workspace_bytes() bytes */
   int64_t workspace_bytes;
@@ -121,8 +129,11 @@ FA2_API int64_t fa2_fwd_sm100_workspace_bytes(const Fa2FwdParams* p);
  *    than FA2_NOALLOC_SCRATCH_BYTES; use fewer splits or fa2_fwd_sm100 with a workspace;
  *  - the array is created when the library's GPU code is loaded and every GPU that loads the
  *    library holds it until the process exits;
- *  - the first call on each device looks up the array's device address (once per device, with
- *    that device current); make that first call before any stream capture;
+ *  - the first call on each device, whatever its num_splits, looks up the array's device
+ *    address (cudaGetSymbolAddress, once per device, with that device current); make that
+ *    first call before any stream capture. Like fa2_fwd_sm100, the first launch of each
+ *    kernel variant on a device also sets its shared-memory attribute
+ *    (cudaFuncSetAttribute); no call allocates;
  *  - all calls share the one array and it keeps the previous call's contents (nothing in it
  *    needs to start at zero: every slot a call reads is written earlier in the same call), so
  *    calls that overlap on the GPU (other streams, other host threads) race on it: serialise

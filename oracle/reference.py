@@ -35,10 +35,14 @@ def _expand_kv(k, v, h_q):
     return k.repeat_interleave(group, dim=1), v.repeat_interleave(group, dim=1)
 
 
-def naive_attention(q, k, v, causal=True, sm_scale=None, dtype=None):
+def naive_attention(q, k, v, causal=True, sm_scale=None, dtype=None, causal_align="top_left"):
     """softmax(Q K^T * sm_scale [+ causal]) V (fa2/reference.py:22-32), per (b, kv-head) unit.
 
     dtype: compute dtype (default: q's dtype, as the reference). Returns that dtype.
+    causal_align: "top_left" is the reference's mask (tril of the [N_q, N_kv] scores).
+    "bottom_right" is an extension the reference does not have (its README lists it out of
+    scope): query i sees keys j <= i + (N_kv - N_q), i.e. tril shifted by N_kv - N_q, the mask
+    FlashAttention uses for N_q != N_kv. Identical to top-left when N_q == N_kv.
     """
     dtype = dtype or q.dtype
     B, H_q, N_q, D = q.shape
@@ -56,7 +60,8 @@ def naive_attention(q, k, v, causal=True, sm_scale=None, dtype=None):
             if causal:
                 if mask is None:
                     n_q, n_kv = s.shape[-2:]
-                    mask = torch.ones(n_q, n_kv, dtype=torch.bool, device=q.device).tril()
+                    shift = n_kv - n_q if causal_align == "bottom_right" else 0
+                    mask = torch.ones(n_q, n_kv, dtype=torch.bool, device=q.device).tril(diagonal=shift)
                 s = s.masked_fill(~mask, float("-inf"))
             out[b, h * group:(h + 1) * group] = torch.softmax(s, dim=-1) @ vs
     return out

@@ -89,9 +89,32 @@ def test_check_accepts_valid():
     (dict(q_stride=(8 * 100 * 128, 100 * 128, 128, 2)), _lib.FA2_ERR_LAYOUT),  # d stride != 1
     (dict(k_stride=(2 * 100 * 130, 100 * 130, 130, 1)), _lib.FA2_ERR_LAYOUT),  # 260-byte rows
     (dict(v_ptr=0x3002), _lib.FA2_ERR_LAYOUT),            # misaligned base
+    (dict(Nq=200, Nkv=100, causal_align=1), _lib.FA2_ERR_SHAPE),  # bottom-right needs N_q <= N_kv
+    (dict(causal_align=2), _lib.FA2_ERR_SHAPE),           # unknown alignment
+    (dict(num_splits=300), _lib.FA2_ERR_SHAPE),           # more than 256 splits
 ])
 def test_check_rejects(kw, status):
     assert _lib.check(params(**kw)) == status
+
+
+def test_bottom_right_causal_accepts_shorter_queries():
+    assert _lib.check(params(Nq=7, Nkv=1000, causal_align=_lib.FA2_CAUSAL_BOTTOM_RIGHT)) == _lib.FA2_OK
+    assert _lib.check(params(Nq=7, Nkv=1000, causal_align=_lib.FA2_CAUSAL_TOP_LEFT)) == _lib.FA2_ERR_SHAPE
+    # non-causal calls ignore the alignment
+    assert _lib.check(params(causal=0, Nq=300, Nkv=100, causal_align=_lib.FA2_CAUSAL_BOTTOM_RIGHT)) == _lib.FA2_OK
+
+
+@pytest.mark.parametrize("kw", [dict(Hkv=0), dict(Hq=-(2 ** 31), Hkv=-1), dict(Hq=6, Hkv=4), dict(batch=0)])
+def test_split_entry_points_reject_bad_heads_without_dividing(kw):
+    """Shapes that the split-KV planner would divide by (H_kv = 0, INT_MIN / -1) come back as
+    error codes from every entry point; no host arithmetic fault. Host only: the noalloc entry
+    point validates before it touches the device."""
+    L = _lib.lib()
+    p = params(causal=0, Nq=4, Nkv=4096, num_splits=4, **kw)
+    assert _lib.workspace_bytes(p) == 0
+    assert _lib.check(p) in (_lib.FA2_ERR_SHAPE, _lib.FA2_ERR_GQA)
+    assert L.fa2_fwd_sm100_noalloc(ctypes.byref(p), None) in (_lib.FA2_ERR_SHAPE, _lib.FA2_ERR_GQA)
+    assert L.fa2_fwd_sm100(ctypes.byref(p), None) in (_lib.FA2_ERR_SHAPE, _lib.FA2_ERR_GQA)
 
 
 def test_should_pack_gqa_follows_tile_efficiency():
@@ -128,6 +151,10 @@ def test_reference_asserts_kept():
     q, k, v = cpu_qkv()
     with pytest.raises(AssertionError):
         attention(q, k[:, :, :8], v[:, :, :8], causal=True)       # causal with N_q != N_kv
+    with pytest.raises(AssertionError):                            # bottom-right: N_q > N_kv
+        attention(q, k[:, :, :8], v[:, :, :8], causal=True, causal_align="bottom_right")
+    with pytest.raises(AssertionError):
+        attention(q, k, v, causal=True, causal_align="diagonal")
     with pytest.raises(AssertionError):
         attention(q.float(), k.float(), v.float())                 # fp32 is not supported
     with pytest.raises(AssertionError):
@@ -166,6 +193,9 @@ def test_auto_num_splits():
     assert auto_num_splits(4, 32, 1, 65536, 4, 4, False) == 8           # 32 CTAs -> 4 pairs each
     assert auto_num_splits(2, 8, 200, 8192, 1, 1, False) == 9           # 200 rows (no pairs): 16 CTAs -> 144
     assert auto_num_splits(1, 8, 1, 512, 8, 8, False) == 1              # too few K/V tiles
+    # bottom-right causal decode / chunked prefill splits like the unmasked case
+    assert auto_num_splits(4, 32, 1, 65536, 4, 4, True, causal_align="bottom_right") == 8
+    assert auto_num_splits(4, 32, 1, 65536, 4, 4, True) == 1            # top-left: N_q == N_kv only
 
 
 def test_ablation_switches_exist_in_the_kernel_source():

@@ -45,10 +45,21 @@ def errors(out, ref):
     return diff.max().item()
 
 
+def sdpa(q, k, v, causal, causal_align="top_left", **kw):
+    """torch SDPA at the input dtype: the tolerance yardstick of the reference's rule. Its
+    is_causal mask is top-left; the bottom-right mask is passed explicitly."""
+    if causal and causal_align == "bottom_right":
+        n_q, n_kv = q.shape[2], k.shape[2]
+        mask = torch.ones(n_q, n_kv, dtype=torch.bool, device=q.device).tril(diagonal=n_kv - n_q)
+        return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True, **kw)
+    return F.scaled_dot_product_attention(q, k, v, is_causal=causal, enable_gqa=True, **kw)
+
+
 def check_against_oracle(q, k, v, causal, **kw):
-    ref = naive_attention(q, k, v, causal=causal, dtype=torch.float64)
+    align = kw.get("causal_align", "top_left")
+    ref = naive_attention(q, k, v, causal=causal, dtype=torch.float64, causal_align=align)
     ours = attention(q, k, v, causal=causal, **kw)
-    theirs = F.scaled_dot_product_attention(q, k, v, is_causal=causal, enable_gqa=True)
+    theirs = sdpa(q, k, v, causal, align)
     torch.cuda.synchronize()
     e_ours, e_sdpa = errors(ours, ref), errors(theirs, ref)
     assert torch.isfinite(ours).all()
@@ -201,6 +212,18 @@ def config_inputs(c):
 def test_baseline_config_parity(name):
     c = CONFIGS[name]
     check_against_oracle(*config_inputs(c), c["causal"])
+
+
+# Full-size shapes of the other dtype at each head dim. They run every compiled exp2 path on
+# unmasked tiles: D=64 bf16 puts pairs 7 and 15 of each chunk on the FMA-pipe polynomial
+# (degree 3), D=128 fp16 pairs 3, 7, 11 and 15 (degree 4); masked tiles use the MUFU only.
+@pytest.mark.parametrize("name,shape", [
+    ("full_long_bf16", dict(B=2, Hq=32, Hkv=32, N=16384, D=64, dtype=torch.bfloat16, causal=False, scale=0.5)),
+    ("headline_fp16", dict(B=2, Hq=32, Hkv=8, N=8192, D=128, dtype=torch.float16, causal=True)),
+    ("mha_causal_d64_bf16", dict(B=4, Hq=16, Hkv=16, N=4096, D=64, dtype=torch.bfloat16, causal=True)),
+])
+def test_full_size_other_dtype_parity(name, shape):
+    check_against_oracle(*config_inputs(shape), shape["causal"])
 
 
 def test_pack_tail_config_both_modes_bit_equal():
@@ -361,3 +384,39 @@ def test_split_kv_dual_pairs(num_splits, N_kv):
 @pytest.mark.parametrize("D", [64, 128])
 def test_split_kv_dual_fp16_unpacked(D):
     check_against_oracle(*make_cuda_qkv(2, 4, 4, 100, 3000, D, torch.float16), causal=False, num_splits=4)
+
+
+def test_split_kv_combine_more_slices_than_grid_y():
+    """More (batch, head block) slices than a grid's y extent allows (65535): the merge kernel
+    strides over them. 1100 x 64 unpacked query heads = 70400 slices."""
+    q, k, v = make_cuda_qkv(1100, 64, 1, 1, 1024, 128, torch.bfloat16, seed=5)
+    check_against_oracle(q, k, v, causal=False, pack_gqa=False, num_splits=2)
+
+
+# ------------------------------------------------------------- bottom-right causal mask
+# Extension beyond the reference (whose wrapper asserts N_q == N_kv under causal and whose
+# README lists bottom-right alignment out of scope): query i sees keys j <= i + N_kv - N_q,
+# the decode / chunked-prefill mask. The oracle applies the same shifted tril.
+@pytest.mark.parametrize("N_q", [1, 7, 300])
+@pytest.mark.parametrize("N_kv", [1000, 8192])
+@pytest.mark.parametrize("D,dtype", [(128, torch.bfloat16), (64, torch.float16)])
+def test_bottom_right_causal(N_q, N_kv, D, dtype):
+    q, k, v = make_cuda_qkv(2, 32, 8, N_q, N_kv, D, dtype, seed=N_q + N_kv)
+    check_against_oracle(q, k, v, True, causal_align="bottom_right")                  # auto split-KV
+    check_against_oracle(q, k, v, True, causal_align="bottom_right", num_splits=1)
+    check_against_oracle(q, k, v, True, causal_align="bottom_right", pack_gqa=False, num_splits=3)
+
+
+def test_bottom_right_equals_top_left_when_lengths_match():
+    q, k, v = make_cuda_qkv(2, 8, 2, 777, 777, 128, torch.bfloat16)
+    assert torch.equal(attention(q, k, v, causal=True, causal_align="bottom_right"), attention(q, k, v, causal=True))
+
+
+def test_bottom_right_chunked_prefill_matches_full_causal_rows():
+    """A chunk of queries at the end of a sequence, attended with the bottom-right mask against
+    the whole K/V, gives the last rows of the full causal run (same values within the bar;
+    the tile boundaries differ, so not bit for bit)."""
+    q, k, v = make_cuda_qkv(1, 16, 4, 2048, 2048, 128, torch.bfloat16, seed=9)
+    full = attention(q, k, v, causal=True)
+    tail = attention(q[:, :, -300:], k, v, causal=True, causal_align="bottom_right")
+    assert (tail.float() - full[:, :, -300:].float()).abs().max().item() < 2e-2

@@ -88,3 +88,19 @@ def test_make_qkv_spikes():
     _, k, _ = make_qkv(1, 2, 1, 200, 200, 128, torch.float32, spike_frac=0.01)
     n = int((k.abs() == 8.0).sum())
     assert n == int(k.numel() * 0.01)
+
+
+@pytest.mark.parametrize("N_q,N_kv", [(1, 9), (5, 13), (13, 13)])
+def test_naive_bottom_right_mask(N_q, N_kv):
+    """The bottom-right extension: query i sees keys j <= i + N_kv - N_q (checked against an
+    explicit softmax over the visible keys of each row); equal to top-left when N_q == N_kv."""
+    q, k, v = make_qkv(1, 4, 2, N_q, N_kv, 16, torch.float64, seed=3)
+    out = naive_attention(q, k, v, causal=True, causal_align="bottom_right")
+    ke, ve = k.repeat_interleave(2, dim=1), v.repeat_interleave(2, dim=1)
+    for i in range(N_q):
+        vis = i + N_kv - N_q + 1
+        s = (q[:, :, i:i + 1] @ ke[:, :, :vis].transpose(-1, -2)) / 4.0
+        want = torch.softmax(s, dim=-1) @ ve[:, :, :vis]
+        torch.testing.assert_close(out[:, :, i:i + 1], want, rtol=1e-12, atol=1e-12)
+    if N_q == N_kv:
+        assert torch.equal(out, naive_attention(q, k, v, causal=True))

@@ -5,8 +5,10 @@ being captured, runtimes that own all device allocations, plugins handed only in
 output pointers): the split-KV forward keeps its fp32 partials in a static device array
 that belongs to the library instead of a caller workspace. The test compares it with the
 regular entry point fa2_fwd_sm100 (given a torch-allocated workspace) on the same split
-configuration, on two calls in a row (the second call finds the first call's data in the
-shared array), and checks that a call needing more than the array is refused.
+configuration, on two calls in a row. Between them an unrelated call (other data, other split
+layout) leaves its own partials in the shared array, so a slot that a call read before writing
+it would show up as a mismatch. It also checks that a call needing more than the array is
+refused.
 This file sorts last so a run that stops at the first failure has run every other test.
 """
 
@@ -45,13 +47,22 @@ def test_noalloc_matches_regular_entry_point_twice():
     assert _lib.workspace_bytes(p) <= _lib.NOALLOC_SCRATCH_BYTES
     assert L.fa2_fwd_sm100(ctypes.byref(p), ctypes.c_void_p(stream)) == _lib.FA2_OK
 
-    for _ in range(2):  # two calls in a row on the shared static scratch
+    # an unrelated call: different values, 8 splits over another K/V length, 12 query rows
+    q2, k2, v2 = make_qkv(2, 32, 8, 12, 9000, 128, torch.bfloat16, seed=12, device="cuda")
+    other = torch.empty_like(q2)
+
+    for i in range(2):  # two calls in a row on the shared static scratch
         out = torch.full_like(q, float("nan"))
         pn = _params(q, k, v, out, splits)
         assert L.fa2_fwd_sm100_noalloc(ctypes.byref(pn), ctypes.c_void_p(stream)) == _lib.FA2_OK
         torch.cuda.synchronize()
         assert torch.isfinite(out).all()
         assert torch.equal(out, ref)
+        if i == 0:
+            po = _params(q2, k2, v2, other, 8)
+            assert L.fa2_fwd_sm100_noalloc(ctypes.byref(po), ctypes.c_void_p(stream)) == _lib.FA2_OK
+            torch.cuda.synchronize()
+            assert torch.isfinite(other).all()
 
     # and both agree with the fp64 oracle within the suite's bar
     from oracle.reference import naive_attention

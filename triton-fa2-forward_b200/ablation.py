@@ -16,8 +16,9 @@ Every variant computes the full attention (no work is skipped); they differ only
   d64_bf16_all_mufu   every exp2 on the MUFU at D=64 bf16
   emu_12, emu_12_pairs_7, emu_37   12.5% (pairs 1,9 / 7,15) or 37.5% on the FMA pipe at D=128
   p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
-  no_spec_max    the row max taken before any exp2 (FA2_SPEC_MAX=0) instead of in parallel with
-                 the first chunks, with a redo when a max moves
+  no_spec_max    the row max taken before any exp2 at both head dims (shipped: at D=128 only)
+  spec_max       P's first chunks computed with the current reference max while the row max is
+                 taken, with a redo when a max moves, at both head dims (shipped: at D=64 only)
   two_issuers    one MMA-issuing thread per Q tile (FA2_TWO_ISSUERS=1) instead of one for both
   stages_4, stages_2   K/V ring of 4 (2) slots at D=128, 8 (4) at D=64 (shipped: 3 and 8); the
                  4-slot ring only fits with one O staging chunk per warp
@@ -75,7 +76,8 @@ COMPILED = {
     "d64_bf16_all_mufu": ["-DFA2_EMU_MASK_D64_BF16=0x0u"],
     "emu_37": ["-DFA2_EMU_MASK_D128=0x2A2Au"],
     "p_split_2": ["-DFA2_P_SPLIT=2"],
-    "no_spec_max": ["-DFA2_SPEC_MAX=0"],
+    "no_spec_max": ["-DFA2_SPEC_MAX_D128=0", "-DFA2_SPEC_MAX_D64=0"],
+    "spec_max": ["-DFA2_SPEC_MAX_D128=1", "-DFA2_SPEC_MAX_D64=1"],
     "two_issuers": ["-DFA2_TWO_ISSUERS=1"],
     "stages_4": ["-DFA2_STAGES_D128=4", "-DFA2_STAGES_D64=8", "-DFA2_STG_FULL=0"],
     "stages_2": ["-DFA2_STAGES_D128=2", "-DFA2_STAGES_D64=4"],

@@ -140,11 +140,17 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_MMA_SPIN
 #define FA2_MMA_SPIN 0  // 1: the MMA thread polls its barriers without suspending (measured: no gain)
 #endif
-#ifndef FA2_SPEC_MAX
-// 1: on unmasked steps with a finite reference max, P is computed with the current reference
-// max while the row max is taken; a row whose max moves past the threshold (rare after the
-// first tile) redoes its P before the hand-off. Same values as taking the max first.
-#define FA2_SPEC_MAX 1
+// Speculative max, per head dim. 1: on unmasked steps with a finite reference max, P is
+// computed with the current reference max while the row max is taken; a row whose max moves
+// past the threshold (rare after the first tile) redoes its P before the hand-off. Same values
+// as taking the max first. Measured +4..6% at D = 64 (non-causal); at D = 128 it is within
+// +-1% and its redo path keeps the scores live next to the P chunks, which spills registers
+// (80-92 bytes on every bf16 build), so D = 128 takes the max first.
+#ifndef FA2_SPEC_MAX_D128
+#define FA2_SPEC_MAX_D128 0
+#endif
+#ifndef FA2_SPEC_MAX_D64
+#define FA2_SPEC_MAX_D64 1
 #endif
 #ifndef FA2_STAGES_D128
 // K/V ring slots of 32 KiB at D = 128 (the split-KV build uses 4). A 4th slot fits only with
@@ -174,6 +180,10 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
 #endif
+template <int D>
+__host__ __device__ constexpr bool spec_max() {
+  return D == 128 ? FA2_SPEC_MAX_D128 != 0 : FA2_SPEC_MAX_D64 != 0;
+}
 template <int D, bool BF16>
 __host__ __device__ constexpr uint32_t emu_pair_mask() {
   return D == 128 ? static_cast<uint32_t>(FA2_EMU_MASK_D128)
@@ -274,6 +284,10 @@ inline FastDiv make_fastdiv(uint32_t d) {
 
 struct KArgs {
   int n_q, n_kv, group, pack, hblocks;  // hblocks = H_q / pack
+  // Causal: query position i sees key columns c <= i + causal_off. 0 is the reference's
+  // top-left alignment (N_q == N_kv); N_kv - N_q aligns the last query with the last key
+  // (bottom-right, for chunked prefill and decode with N_q <= N_kv).
+  int causal_off;
   int pack_shift;                       // pack == 1 << pack_shift (pack divides 128)
   FastDiv div_xblocks, div_hblocks, div_group;
   float qk_scale;
@@ -298,13 +312,13 @@ struct KArgs {
 };
 
 // K/V tiles a CTA of 256-row block mb visits (>= 1): its causal band end, or all of N_kv.
-// pack == 1 << pack_shift.
+// pack == 1 << pack_shift; causal_off >= 0 is the bottom-right shift (KArgs::causal_off).
 template <bool CAUSAL>
-__host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, int pack_shift) {
+__host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, int pack_shift, int causal_off) {
   int kv_end = n_kv;
   if (CAUSAL) {
     const int last_pos = min((mb * 256 + 255) >> pack_shift, n_q - 1);
-    kv_end = min(last_pos + 1, n_kv);
+    kv_end = min(last_pos + 1 + causal_off, n_kv);
   }
   return (kv_end + 127) / 128;
 }
@@ -339,7 +353,7 @@ __device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
   u.hkv = static_cast<int>(a.div_group.div(static_cast<uint32_t>(u.hq0)));
   static_assert(Q_TILES * BM == 256 && BN == 128, "cta_kv_tiles assumes 256-row CTAs, 128-row K/V tiles");
   u.row0 = mb * (Q_TILES * BM);
-  const int J_cta = cta_kv_tiles<CAUSAL>(mb, a.n_q, a.n_kv, a.pack_shift);
+  const int J_cta = cta_kv_tiles<CAUSAL>(mb, a.n_q, a.n_kv, a.pack_shift, a.causal_off);
   u.j0 = 0;
   u.j0b = 0;
   u.J = J_cta;
@@ -865,11 +879,11 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
         tc_fence_after();
         const int col0 = (kv_base + j) * BN;
-        const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0);
+        const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0 + a.causal_off);
         const bool need_pad = (col0 + BN > a.n_kv);
         const bool masked = need_causal || need_pad;  // uniform over the tile's warps
         int lim = a.n_kv - 1 - col0;                  // last visible column of this tile, relative
-        if (CAUSAL) lim = min(lim, pos - col0);
+        if (CAUSAL) lim = min(lim, pos + a.causal_off - col0);
 
         // This warp's scores of the row in one batch of loads and a single wait.
         uint32_t s[NCH][32];
@@ -885,7 +899,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < NCH; ++c) reg_fence32(s[c]);
-        if (FA2_SPEC_MAX && !masked && j > 0 && __all_sync(0xffffffffu, m_use != -INFINITY)) {
+        if (spec_max<D>() && !masked && j > 0 && __all_sync(0xffffffffu, m_use != -INFINITY)) {
           // P with the current reference max while the row max is taken (the two are independent
           // and use different pipes); the threshold test then runs before the hand-off.
           float m_cand = row_max_chunks(s) * qk_scale;
@@ -1124,8 +1138,10 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // --------------------------------------------------------------- split-KV combine
 // One warp per packed row: O = sum_s w_s O_s / sum_s w_s with w_s = 2^(lse_s - max lse), over
 // the splits that cover this row's 256-row block, written in the input dtype with o's strides.
+// Grid: x covers the packed rows in blocks of 8; y strides over the (batch, head block) slices
+// (gridDim.y is capped at 65535 by the host, xblocks may be larger).
 struct CombineArgs {
-  int n_q, n_kv, pack, pack_shift, hblocks, rows_pad, num_splits, split_tiles;
+  int n_q, n_kv, pack, pack_shift, hblocks, rows_pad, num_splits, split_tiles, causal_off, xblocks;
   int64_t ob, oh, on;  // output element strides (b, h, n); d stride is 1
 };
 
@@ -1136,36 +1152,37 @@ fa2_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int R = blockIdx.x * 8 + warp;  // packed row within the (batch, head block) slice
   if (R >= c.n_q * c.pack) return;
-  const int x = blockIdx.y;
-  const int b = x / c.hblocks;
-  const int h = (x % c.hblocks) * c.pack + R % c.pack;
   const int pos = R / c.pack;
-  const int J_cta = cta_kv_tiles<CAUSAL>(R / 256, c.n_q, c.n_kv, c.pack_shift);
+  const int J_cta = cta_kv_tiles<CAUSAL>(R / 256, c.n_q, c.n_kv, c.pack_shift, c.causal_off);
   const int ns = min(c.num_splits, (J_cta + c.split_tiles - 1) / c.split_tiles);
-  const int64_t xs = static_cast<int64_t>(gridDim.y);
-  float mx = -INFINITY;
-  for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, lse_part[(sp * xs + x) * c.rows_pad + R]);
+  const int64_t xs = static_cast<int64_t>(c.xblocks);
   constexpr int PER = D / 32;  // columns per lane
-  float acc[PER];
+  for (int x = static_cast<int>(blockIdx.y); x < c.xblocks; x += static_cast<int>(gridDim.y)) {
+    const int b = x / c.hblocks;
+    const int h = (x % c.hblocks) * c.pack + R % c.pack;
+    float mx = -INFINITY;
+    for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, lse_part[(sp * xs + x) * c.rows_pad + R]);
+    float acc[PER];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) acc[i] = 0.0f;
-  float wsum = 0.0f;
-  for (int sp = 0; sp < ns; ++sp) {
-    const int64_t slot = (sp * xs + x) * c.rows_pad + R;
-    const float lse = lse_part[slot];
-    if (lse == -INFINITY) continue;  // this split saw no visible column of the row
-    const float w = exp2f(lse - mx);
-    wsum += w;
-    const float* src = o_part + slot * D + lane * PER;
+    for (int i = 0; i < PER; ++i) acc[i] = 0.0f;
+    float wsum = 0.0f;
+    for (int sp = 0; sp < ns; ++sp) {
+      const int64_t slot = (sp * xs + x) * c.rows_pad + R;
+      const float lse = lse_part[slot];
+      if (lse == -INFINITY) continue;  // this split saw no visible column of the row
+      const float w = exp2f(lse - mx);
+      wsum += w;
+      const float* src = o_part + slot * D + lane * PER;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] = fmaf(w, src[i], acc[i]);
-  }
-  const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
-  uint16_t* dst = reinterpret_cast<uint16_t*>(out) + b * c.ob + h * c.oh + pos * c.on + lane * PER;
+      for (int i = 0; i < PER; ++i) acc[i] = fmaf(w, src[i], acc[i]);
+    }
+    const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+    uint16_t* dst = reinterpret_cast<uint16_t*>(out) + b * c.ob + h * c.oh + pos * c.on + lane * PER;
 #pragma unroll
-  for (int i = 0; i < PER; i += 2) {
-    const uint32_t pk = cvt_pack2<BF16>(acc[i] * inv, acc[i + 1] * inv);
-    *reinterpret_cast<uint32_t*>(dst + i) = pk;
+    for (int i = 0; i < PER; i += 2) {
+      const uint32_t pk = cvt_pack2<BF16>(acc[i] * inv, acc[i + 1] * inv);
+      *reinterpret_cast<uint32_t*>(dst + i) = pk;
+    }
   }
 }
 
@@ -1235,17 +1252,24 @@ struct SplitPlan {
   int64_t bytes = 0;
 };
 
+// Split layout of a call. Shapes the validation would reject (which could divide by zero
+// here) get the unsplit plan, so the caller's own check reports them.
 SplitPlan plan_splits(const Fa2FwdParams* p) {
   SplitPlan sp;
   if (p->num_splits <= 1) return sp;
+  if (p->batch < 1 || p->heads_q < 1 || p->heads_kv < 1 || p->heads_q % p->heads_kv != 0 || p->seqlen_q < 0 ||
+      p->seqlen_kv < 1) {
+    return sp;
+  }
   const int group = p->heads_q / p->heads_kv;
   const int pack = p->pack_gqa ? group : 1;
   const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
   const int mblocks = static_cast<int>((rows + 255) / 256);
   const int j_max = (p->seqlen_kv + 127) / 128;
-  // Dual mode: every query row sits in the CTA's first Q tile (short queries, no causal
-  // band), so the second tile slot walks another split of the same rows; splits come in pairs.
-  sp.dual = (!p->causal && rows <= 128) ? 1 : 0;
+  // Dual mode: every query row sits in the CTA's first Q tile (short queries), so the second
+  // tile slot walks another split of the same rows; splits come in pairs. Under a causal mask
+  // the tiles of a split past a row's last visible key are fully masked (exact zeros).
+  sp.dual = (rows <= 128) ? 1 : 0;
   sp.num_splits = sp.dual ? ((p->num_splits + 1) / 2) * 2 : p->num_splits;
   sp.grid_z = sp.dual ? sp.num_splits / 2 : sp.num_splits;
   sp.split_tiles = (j_max + sp.num_splits - 1) / sp.num_splits;
@@ -1300,6 +1324,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.pack_shift = 0;
   while ((1 << ka.pack_shift) < pack) ++ka.pack_shift;  // pack divides 128: a power of two
   ka.hblocks = p->heads_q / pack;
+  ka.causal_off = (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT) ? p->seqlen_kv - p->seqlen_q : 0;
   ka.qk_scale = p->qk_scale;
   ka.err = p->err_flag;
   ka.gate = p->gate;
@@ -1347,10 +1372,12 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
     ca.rows_pad = sp.rows_pad;
     ca.num_splits = sp.num_splits;
     ca.split_tiles = sp.split_tiles;
+    ca.causal_off = ka.causal_off;
+    ca.xblocks = sp.xblocks;
     ca.ob = p->o_stride[0];
     ca.oh = p->o_stride[1];
     ca.on = p->o_stride[2];
-    const dim3 cgrid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(sp.xblocks));
+    const dim3 cgrid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(sp.xblocks < 65535 ? sp.xblocks : 65535));
     fa2::fa2_combine_kernel<D, CAUSAL, BF16><<<cgrid, 256, 0, stream>>>(ka.o_part, ka.lse_part, p->o, ca);
     if (cudaGetLastError() != cudaSuccess) return FA2_ERR_LAUNCH;
   }
@@ -1390,7 +1417,7 @@ const char* fa2_sm100_strerror(int status) {
   switch (status) {
     case FA2_OK: return "ok";
     case FA2_ERR_NULL: return "a required pointer is NULL";
-    case FA2_ERR_SHAPE: return "invalid shape (sizes, batch/head_dim mismatch, or causal with N_q != N_kv)";
+    case FA2_ERR_SHAPE: return "invalid shape (sizes, batch/head_dim mismatch, causal top-left with N_q != N_kv, or causal bottom-right with N_q > N_kv)";
     case FA2_ERR_DTYPE: return "dtype must be fp16 or bf16";
     case FA2_ERR_HEAD_DIM: return "head_dim not supported by the compiled sm_100a kernels (64, 128)";
     case FA2_ERR_GQA: return "H_q must be divisible by H_kv";
@@ -1427,10 +1454,16 @@ int fa2_fwd_sm100_config(int32_t head_dim, int32_t* block_m, int32_t* block_n, i
   return FA2_OK;
 }
 
-int fa2_fwd_sm100_check(const Fa2FwdParams* p) {
+}  // extern "C"
+
+namespace {
+// Everything fa2_fwd_sm100_check validates except the split-KV workspace.
+int check_core(const Fa2FwdParams* p) {
   if (p == nullptr || p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr) return FA2_ERR_NULL;
   if (p->batch < 1 || p->heads_q < 1 || p->heads_kv < 1 || p->seqlen_q < 0 || p->seqlen_kv < 1) return FA2_ERR_SHAPE;
-  if (p->causal && p->seqlen_q != p->seqlen_kv) return FA2_ERR_SHAPE;
+  if (p->causal_align != FA2_CAUSAL_TOP_LEFT && p->causal_align != FA2_CAUSAL_BOTTOM_RIGHT) return FA2_ERR_SHAPE;
+  if (p->causal && p->causal_align == FA2_CAUSAL_TOP_LEFT && p->seqlen_q != p->seqlen_kv) return FA2_ERR_SHAPE;
+  if (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT && p->seqlen_q > p->seqlen_kv) return FA2_ERR_SHAPE;
   if (p->dtype != FA2_DTYPE_FP16 && p->dtype != FA2_DTYPE_BF16) return FA2_ERR_DTYPE;
   if (p->head_dim != 64 && p->head_dim != 128) return FA2_ERR_HEAD_DIM;
   if (p->heads_q % p->heads_kv != 0) return FA2_ERR_GQA;
@@ -1448,8 +1481,17 @@ int fa2_fwd_sm100_check(const Fa2FwdParams* p) {
     return FA2_ERR_LAYOUT;
   }
   if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o)) return FA2_ERR_LAYOUT;
+  if (p->num_splits > 256) return FA2_ERR_SHAPE;
+  return FA2_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int fa2_fwd_sm100_check(const Fa2FwdParams* p) {
+  const int rc = check_core(p);
+  if (rc != FA2_OK) return rc;
   if (p->num_splits > 1) {
-    if (p->num_splits > 256) return FA2_ERR_SHAPE;
     if (p->workspace == nullptr || !aligned16(p->workspace) ||
         p->workspace_bytes < plan_splits(p).bytes) {
       return FA2_ERR_WORKSPACE;
@@ -1493,22 +1535,25 @@ void* g_noalloc_addr[kMaxDevices] = {};
 }  // namespace
 
 extern "C" int fa2_fwd_sm100_noalloc(const Fa2FwdParams* p, void* stream) {
-  if (p == nullptr) return FA2_ERR_NULL;
+  // Shapes first: the split plan below divides by the head counts.
+  const int rc = check_core(p);
+  if (rc != FA2_OK) return rc;
   Fa2FwdParams q = *p;
   q.workspace = nullptr;
   q.workspace_bytes = 0;
-  if (q.num_splits > 1) {
-    if (plan_splits(&q).bytes > FA2_NOALLOC_SCRATCH_BYTES) return FA2_ERR_SCRATCH_LIMIT;
-    int dev = -1;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FA2_ERR_DEVICE;
-    if (g_noalloc_addr[dev] == nullptr) {
-      // Set-up, once per device, with that device current (done before any launch here).
-      void* addr = nullptr;
-      if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || addr == nullptr) {
-        return FA2_ERR_DEVICE;
-      }
-      g_noalloc_addr[dev] = addr;
+  if (q.num_splits > 1 && plan_splits(&q).bytes > FA2_NOALLOC_SCRATCH_BYTES) return FA2_ERR_SCRATCH_LIMIT;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FA2_ERR_DEVICE;
+  if (g_noalloc_addr[dev] == nullptr) {
+    // Set-up on the first call on each device, whatever its num_splits, with that device
+    // current and before any launch of this call.
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || addr == nullptr) {
+      return FA2_ERR_DEVICE;
     }
+    g_noalloc_addr[dev] = addr;
+  }
+  if (q.num_splits > 1) {
     q.workspace = g_noalloc_addr[dev];
     q.workspace_bytes = FA2_NOALLOC_SCRATCH_BYTES;
   }

@@ -10,10 +10,13 @@ import os
 LIB_NAME = "libfa2_sm100.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 FA2_DTYPE_FP16 = 0
 FA2_DTYPE_BF16 = 1
+
+FA2_CAUSAL_TOP_LEFT = 0
+FA2_CAUSAL_BOTTOM_RIGHT = 1
 
 FA2_OK = 0
 FA2_ERR_NULL = 1
@@ -71,7 +74,7 @@ class Fa2FwdParams(ctypes.Structure):
         ("timeout_cycles", ctypes.c_int64),
         ("gate", ctypes.c_void_p),
         ("num_splits", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("causal_align", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_int64),
     ]
@@ -143,7 +146,7 @@ def config(head_dim):
 def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stride,
                 batch, heads_q, heads_kv, seqlen_q, seqlen_kv, head_dim, dtype, causal,
                 pack_gqa, qk_scale, err_flag=0, timeout_cycles=0, gate=0, num_splits=1,
-                workspace=0, workspace_bytes=0):
+                workspace=0, workspace_bytes=0, causal_align=FA2_CAUSAL_TOP_LEFT):
     p = Fa2FwdParams()
     p.q, p.k, p.v, p.o = q_ptr, k_ptr, v_ptr, o_ptr
     p.q_stride[:] = list(q_stride)
@@ -158,6 +161,7 @@ def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stri
     p.timeout_cycles = int(timeout_cycles)
     p.gate = gate or None
     p.num_splits = int(num_splits)
+    p.causal_align = int(causal_align)
     p.workspace = workspace or None
     p.workspace_bytes = int(workspace_bytes)
     return p

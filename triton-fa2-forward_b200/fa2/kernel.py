@@ -8,7 +8,7 @@ Same public surface as the reference:
     _default_config(head_dim, on_cuda)                               fa2/kernel.py:186-195
 
 q: [B, H_q, N_q, D]; k, v: [B, H_kv, N_kv, D] (any strides); H_q % H_kv == 0; fp16/bf16;
-returns out = softmax(q k^T * sm_scale [+ top-left causal mask]) v with q's strides.
+returns out = softmax(q k^T * sm_scale [+ causal mask]) v with q's strides.
 The computation is the hand-written sm_100a CUDA kernel in csrc/fa2_fwd_sm100.cu, reached
 through the C ABI of include/fa2_sm100.h. There is no Triton and no CPU path: tensors not
 on an sm_100 CUDA device raise RuntimeError.
@@ -21,9 +21,18 @@ Differences from the reference that do not change results:
     so a group that divides the hinted block_m but not 128 simply runs unpacked.
   * head_dim 16 and 32 run the 64 kernel on zero-padded copies (extra zero columns add
     nothing to QK^T and produce zero output columns that are dropped).
+
+Extensions (keyword arguments the reference does not have; their defaults keep its behaviour):
+  * causal_align="bottom_right": the causal mask lines the last query up with the last key
+    (query i sees keys j <= i + N_kv - N_q), for chunked prefill and decode with N_q <= N_kv.
+    The default "top_left" is the reference's mask and keeps its N_q == N_kv assertion.
+  * num_splits: split-KV for short queries against long K/V (auto_num_splits by default).
+  * FA2_SYNC_CHECK=1 in the environment: every call synchronises and raises RuntimeError if
+    the kernel reported a timed-out wait (a debugging aid; calls are asynchronous otherwise).
 """
 
 import math
+import os
 
 import torch
 
@@ -37,6 +46,11 @@ NUM_SMS_B200 = 148
 MAX_SPLITS = 16
 
 _err_words = {}
+CAUSAL_ALIGNS = {"top_left": _lib.FA2_CAUSAL_TOP_LEFT, "bottom_right": _lib.FA2_CAUSAL_BOTTOM_RIGHT}
+
+
+def _sync_check_enabled():
+    return os.environ.get("FA2_SYNC_CHECK", "0") not in ("", "0")
 
 
 def _default_config(head_dim, on_cuda):
@@ -90,14 +104,16 @@ def _strides(t):
     return tuple(int(s) for s in t.stride())
 
 
-def auto_num_splits(batch, heads_q, n_q, n_kv, group, pack, causal, num_sms=NUM_SMS_B200):
+def auto_num_splits(batch, heads_q, n_q, n_kv, group, pack, causal, num_sms=NUM_SMS_B200,
+                    causal_align="top_left"):
     """Split-KV count for a launch (an extension; the reference has no split-KV). Splitting
     pays when the (batch, head block, 256-row block) CTAs cannot fill the GPU and each has a
     long K/V range, i.e. short queries against long K/V. One CTA fits per SM, so the split
     CTAs are kept within one wave (measured: a second partial wave costs more than the split
-    gains), with at least 4 K/V tiles per split. Causal attention has N_q == N_kv and is not
-    split."""
-    if causal:
+    gains), with at least 4 K/V tiles per split. Top-left causal attention has N_q == N_kv and
+    is not split; bottom-right causal with N_q < N_kv is split like the unmasked case (every
+    query sees nearly all of the K/V)."""
+    if causal and (causal_align != "bottom_right" or n_q >= n_kv):
         return 1
     P = pack if pack else 1
     ctas = batch * (heads_q // P) * (-(-(n_q * P) // CTA_ROWS))
@@ -114,7 +130,7 @@ def auto_num_splits(batch, heads_q, n_q, n_kv, group, pack, causal, num_sms=NUM_
     return max(1, min(MAX_SPLITS, num_sms // ctas, tiles // 4))
 
 
-def _launch(q, k, v, out, causal, pack, qk_scale, num_splits=1, timeout_cycles=0):
+def _launch(q, k, v, out, causal, pack, qk_scale, num_splits=1, timeout_cycles=0, align=0):
     B, H_q, N_q, D = q.shape
     H_kv, N_kv = k.shape[1], k.shape[2]
     err = _err_word(q.device)
@@ -124,6 +140,7 @@ def _launch(q, k, v, out, causal, pack, qk_scale, num_splits=1, timeout_cycles=0
         B, H_q, H_kv, N_q, N_kv, D,
         _lib.FA2_DTYPE_BF16 if q.dtype == torch.bfloat16 else _lib.FA2_DTYPE_FP16,
         causal, pack, qk_scale, err.data_ptr(), timeout_cycles, num_splits=num_splits,
+        causal_align=align,
     )
     ws = None
     if num_splits > 1:
@@ -137,26 +154,29 @@ def _launch(q, k, v, out, causal, pack, qk_scale, num_splits=1, timeout_cycles=0
     return rc
 
 
-def _run(q, k, v, out, causal, pack, qk_scale, num_splits=1):
+def _run(q, k, v, out, causal, pack, qk_scale, num_splits=1, align=0):
     with torch.cuda.device(q.device):
-        rc = _launch(q, k, v, out, causal, pack, qk_scale, num_splits)
+        rc = _launch(q, k, v, out, causal, pack, qk_scale, num_splits, align=align)
         if rc == _lib.FA2_ERR_TMA_ENCODE and pack:
             pack = False  # bit-identical result; some stride orders only encode unpacked
-            rc = _launch(q, k, v, out, causal, pack, qk_scale, num_splits)
+            rc = _launch(q, k, v, out, causal, pack, qk_scale, num_splits, align=align)
         if rc in (_lib.FA2_ERR_LAYOUT, _lib.FA2_ERR_TMA_ENCODE):
             # Layout copy (not a compute fallback): TMA needs 16-byte strides/alignment.
             qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
             oc = torch.empty_like(qc)
-            rc = _launch(qc, kc, vc, oc, causal, pack, qk_scale, num_splits)
+            rc = _launch(qc, kc, vc, oc, causal, pack, qk_scale, num_splits, align=align)
             if rc == _lib.FA2_OK:
                 out.copy_(oc)
         if rc != _lib.FA2_OK:
             raise _lib.Fa2Error(rc, _lib.strerror(rc))
+        if _sync_check_enabled():
+            check_device_errors(q.device)
     return out
 
 
 def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
-              num_warps=None, num_stages=None, pack_gqa=None, num_splits=None):
+              num_warps=None, num_stages=None, pack_gqa=None, num_splits=None,
+              causal_align="top_left"):
     """softmax(Q K^T * sm_scale [+ causal mask]) V, fused (fa2/kernel.py:210-260).
 
     q: [B, H_q, N_q, D]; k, v: [B, H_kv, N_kv, D]; returns [B, H_q, N_q, D].
@@ -165,6 +185,8 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
     on torch's current stream, like the reference.
     num_splits (extension, not in the reference): split-KV count; None picks one with
     auto_num_splits (short queries against long K/V), 1 disables it.
+    causal_align (extension): "top_left" (the reference's mask, N_q == N_kv) or
+    "bottom_right" (query i sees keys j <= i + N_kv - N_q; needs N_q <= N_kv).
     """
     assert q.dim() == k.dim() == v.dim() == 4
     B, H_q, N_q, D = q.shape
@@ -173,9 +195,12 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
     assert q.dtype == k.dtype == v.dtype and q.dtype in (torch.float16, torch.bfloat16)
     assert H_q % H_kv == 0, "GQA needs H_q divisible by H_kv"
     assert D in (16, 32, 64, 128), "head_dim must be a power of two in [16, 128]"
-    if causal:
+    assert causal_align in CAUSAL_ALIGNS, f"causal_align must be one of {sorted(CAUSAL_ALIGNS)}"
+    if causal and causal_align == "top_left":
         # Top-left aligned causal mask (prefill), as in the reference.
         assert N_q == N_kv, "causal attention here assumes N_q == N_kv"
+    if causal and causal_align == "bottom_right":
+        assert N_q <= N_kv, "bottom-right causal attention needs N_q <= N_kv"
 
     bm, bn, nw, ns = _default_config(D, q.is_cuda)
     bm, bn = block_m or bm, block_n or bn
@@ -204,8 +229,10 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
         raise RuntimeError("q, k and v must be on the same CUDA device")
 
     if num_splits is None:
-        num_splits = auto_num_splits(B, H_q, N_q, N_kv, group, group if pack else 1, causal)
+        num_splits = auto_num_splits(B, H_q, N_q, N_kv, group, group if pack else 1, causal,
+                                     causal_align=causal_align)
     num_splits = max(1, int(num_splits))
+    align = CAUSAL_ALIGNS[causal_align]
 
     out = torch.empty_like(q)
     if out.numel() == 0:
@@ -214,7 +241,7 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
         pad = (0, 64 - D)
         qp, kp, vp = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
         op = torch.empty_like(qp)
-        _run(qp, kp, vp, op, causal, pack, qk_scale, num_splits)
+        _run(qp, kp, vp, op, causal, pack, qk_scale, num_splits, align=align)
         out.copy_(op[..., :D])
         return out
-    return _run(q, k, v, out, causal, pack, qk_scale, num_splits)
+    return _run(q, k, v, out, causal, pack, qk_scale, num_splits, align=align)
