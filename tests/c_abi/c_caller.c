@@ -56,6 +56,11 @@ int main(void) {
   CHECK(fa2_fwd_sm100_check(&p) == FA2_ERR_GQA, "H_q % H_kv != 0 is rejected");
   fill(&p, 2, 32, 8, 100, 200, 128);
   CHECK(fa2_fwd_sm100_check(&p) == FA2_ERR_SHAPE, "causal with N_q != N_kv is rejected");
+  p.causal_align = FA2_CAUSAL_BOTTOM_RIGHT;
+  CHECK(fa2_fwd_sm100_check(&p) == FA2_OK, "bottom-right causal accepts N_q < N_kv");
+  fill(&p, 2, 32, 8, 300, 200, 128);
+  p.causal_align = FA2_CAUSAL_BOTTOM_RIGHT;
+  CHECK(fa2_fwd_sm100_check(&p) == FA2_ERR_SHAPE, "bottom-right causal rejects N_q > N_kv");
   fill(&p, 2, 32, 8, 8192, 8192, 128);
   p.q_stride[2] = 129; /* not a multiple of 8 elements */
   CHECK(fa2_fwd_sm100_check(&p) == FA2_ERR_LAYOUT, "unaligned stride is rejected");

@@ -244,3 +244,16 @@ def test_row_split_layout_builds(tmp_path):
     res = subprocess.run(cmd, capture_output=True, text=True)
     assert res.returncode == 0, res.stderr[-3000:]
     assert out.stat().st_size > 0
+
+
+def test_integration_doc_ctypes_mirror_matches_the_library():
+    """The ctypes struct that INTEGRATION.md tells a maintainer to paste is exec'd against the
+    built library: its size must be the library's sizeof(Fa2FwdParams)."""
+    doc = open(os.path.join(os.path.dirname(HEADER), "..", "INTEGRATION.md")).read()
+    blocks = re.findall(r"```python\n(.*?)```", doc, flags=re.S)
+    mirror = [b for b in blocks if "class Fa2FwdParams" in b]
+    assert len(mirror) == 1
+    ns = {"LIB_PATH": _lib.LIB_PATH}
+    exec(mirror[0], ns)  # runs the snippet's own size assertion
+    assert ctypes.sizeof(ns["Fa2FwdParams"]) == ctypes.sizeof(_lib.Fa2FwdParams)
+    assert [f[0] for f in ns["Fa2FwdParams"]._fields_] == [f[0] for f in _lib.Fa2FwdParams._fields_]
