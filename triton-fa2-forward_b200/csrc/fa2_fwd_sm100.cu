@@ -180,6 +180,18 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
 #endif
+#ifndef FA2_SEQ_EXP
+// 1: the two softmax warps of a lane quadrant (tile 0 and tile 1, on the same SMSP) take turns
+// on the exponential phase of a step (tile 0 step j, tile 1 step j, tile 0 step j + 1, ...)
+// through a bounded mbarrier hand-shake, so they never compete for the MUFU and issue slots.
+// The loads and row max of one overlap the other's exponentials. 0: no ordering.
+#define FA2_SEQ_EXP 0
+#endif
+#ifndef FA2_FFMA_PASS
+// 1: x = s * qk_scale - m is computed for the whole row in one pass of packed FMAs before the
+// exponentials (no dependency between them); 0: fused into the per-chunk exponential loop.
+#define FA2_FFMA_PASS 0
+#endif
 template <int D>
 __host__ __device__ constexpr bool spec_max() {
   return D == 128 ? FA2_SPEC_MAX_D128 != 0 : FA2_SPEC_MAX_D64 != 0;
@@ -206,6 +218,7 @@ constexpr bool regs_fit() {
 static_assert(regs_fit<128>() && regs_fit<64>(), "register split exceeds the launch budget");
 static_assert(NUM_THREADS * REGS_LAUNCH <= 65536, "launch register budget");
 static_assert(HALVES == 1 || !FA2_TWO_ISSUERS, "two MMA issuers need the 12-warp layout");
+static_assert(HALVES == 1 || !FA2_SEQ_EXP, "the exponential hand-shake needs the 12-warp layout");
 
 // Shared-memory layout of one CTA. SPLIT: the split-KV build, which writes fp32 partials from
 // registers (no O staging) and, streaming K/V from HBM, uses a deeper ring.
@@ -241,7 +254,8 @@ struct Cfg {
   static constexpr int B_P_LATE = 9 + 2 * STAGES;   // [2]  the remaining P_t columns in TMEM
   static constexpr int B_Q_EMPTY = 11 + 2 * STAGES; // [2]  last QK of tile t of a unit retired: Q_t reloadable
   static constexpr int B_XCH = 13 + 2 * STAGES;     // [8]  (HALVES == 2) row-pair exchange of tile t, quadrant q
-  static constexpr int NUM_BARS = 13 + 2 * STAGES + (HALVES == 2 ? 8 : 0);
+  static constexpr int B_SEQ = 13 + 2 * STAGES;     // [8]  (FA2_SEQ_EXP) exponential phase of tile t, quadrant q done
+  static constexpr int NUM_BARS = 13 + 2 * STAGES + ((HALVES == 2 || FA2_SEQ_EXP) ? 8 : 0);
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
@@ -407,11 +421,12 @@ __device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], int c0, int lim) {
 // p = exp2(s * scale - m) for 32 scores: packed to 16 words of (lo, hi) halves for the PV
 // GEMM, and written back into s as fp32 for the row sum. The pairs set in EMU_MASK are
 // computed on the FMA pipe (exp2_poly_x2); the subset depends only on the column index.
-template <bool BF16, uint32_t EMU_MASK>
+template <bool BF16, uint32_t EMU_MASK, bool PRESCALED = false>
 __device__ __forceinline__ void make_p32(uint32_t (&s)[32], uint64_t sc2, uint64_t nm2, uint32_t (&pk)[16]) {
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])), sc2, nm2);
+    const uint64_t s2 = f2_pack(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1]));
+    const uint64_t x2 = PRESCALED ? s2 : f2_fma(s2, sc2, nm2);
     float x0, x1, p0, p1;
     f2_unpack(x2, x0, x1);
     if ((EMU_MASK >> e) & 1u) {
@@ -505,6 +520,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     }
     if constexpr (HALVES == 2) {
       for (int x = 0; x < 8; ++x) mbar_init(bar(C::B_XCH + x), 64);
+    }
+    if constexpr (FA2_SEQ_EXP != 0) {
+      for (int x = 0; x < 8; ++x) mbar_init(bar(C::B_SEQ + x), 32);
     }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(C::B_KV_FULL + s), 1);
@@ -862,7 +880,25 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       return true;
     };
 
+    // FA2_SEQ_EXP: tile 0's warp of this quadrant runs the exponentials of step k after tile 1's
+    // of step k - 1, tile 1's after tile 0's of step k (k counts steps over all units; both tiles
+    // walk the same steps). One arrival per thread on B_SEQ[t][q] when the phase is done.
     int g = 0;  // steps of the units before
+    auto seq_wait = [&](int j) -> bool {
+      if constexpr (FA2_SEQ_EXP == 0) {
+        return true;
+      } else {
+        const int k = g + j;
+        if (t == 0 && k == 0) return true;
+        const int other = (1 - t) * 4 + q;
+        const uint32_t par = static_cast<uint32_t>(t == 0 ? k - 1 : k) & 1u;
+        const bool w = mbar_wait(bar(C::B_SEQ + other), par, a.timeout, a.err);
+        return __all_sync(0xffffffffu, w);
+      }
+    };
+    auto seq_done = [&]() {
+      if constexpr (FA2_SEQ_EXP != 0) mbar_arrive(bar(C::B_SEQ + t * 4 + q));
+    };
     Unit u;
     bool have = get_unit<CAUSAL>(a, 0, u);
     for (int n = 0; ok && have; ++n) {
@@ -909,6 +945,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           // Pass 0 uses the current reference max. If some row's max moved past the threshold
           // (rare), pass 1 moves it, rescales this warp's O_t columns (PV(t, j-1) has retired:
           // S_t(j) was committed after it) and redoes these chunks with the new reference max.
+          if (!seq_wait(j)) { ok = false; break; }
 #pragma unroll 1
           for (int pass = 0;; ++pass) {
 #pragma unroll
@@ -947,6 +984,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(bar(C::B_P_LATE + t));
+          seq_done();
           const uint64_t acc01 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
           float sl0, sl1;
           f2_unpack(acc01, sl0, sl1);
@@ -980,13 +1018,26 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         // m_use = -inf; its p must be exactly 0, not exp2(-inf + inf).
         const float m_safe = (m_use == -INFINITY) ? 0.0f : m_use;
         const uint64_t nm2 = f2_pack(-m_safe, -m_safe);
+        if constexpr (FA2_FFMA_PASS != 0) {
+#pragma unroll
+          for (int c = 0; c < NCH; ++c) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c][2 * e]), __uint_as_float(s[c][2 * e + 1])), sc2, nm2), x0, x1);
+              s[c][2 * e] = __float_as_uint(x0);
+              s[c][2 * e + 1] = __float_as_uint(x1);
+            }
+          }
+        }
+        if (!seq_wait(j)) { ok = false; break; }
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           uint32_t pk[16];
           if (masked) {
-            make_p32<BF16, 0u>(s[c], sc2, nm2, pk);
+            make_p32<BF16, 0u, FA2_FFMA_PASS != 0>(s[c], sc2, nm2, pk);
           } else {
-            make_p32<BF16, emu_pair_mask<D, BF16>()>(s[c], sc2, nm2, pk);
+            make_p32<BF16, emu_pair_mask<D, BF16>(), FA2_FFMA_PASS != 0>(s[c], sc2, nm2, pk);
           }
           tmem_st16(tP + c * 16, pk);
           if (c == P_SPLIT_W - 1) {
@@ -998,6 +1049,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar(C::B_P_LATE + t));
+        seq_done();
 
         // Row sum of the fp32 p (before rounding, as fa2/kernel.py:98), off the critical path.
         uint64_t acc2[4] = {0, 0, 0, 0};
