@@ -14,6 +14,12 @@
  * every other stride must be a multiple of 8 elements (16 bytes) and the base pointers
  * must be 16-byte aligned (TMA rules); otherwise FA2_ERR_LAYOUT is returned and the
  * caller should pass contiguous copies.
+ *
+ * Variable-length batches (cu_seqlens_q != NULL): the sequences are packed along one token
+ * axis, q and o [total_q, H_q, D], k and v [total_kv, H_kv, D] (the layout of
+ * flash_attn_varlen_func). Sequence b owns q rows [cu_seqlens_q[b], cu_seqlens_q[b + 1]) and
+ * k/v rows [cu_seqlens_kv[b], cu_seqlens_kv[b + 1]); seqlen_q / seqlen_kv are the largest
+ * lengths, and the (b, h, n, d) strides give the token axis as n (the b stride is unused).
  */
 #ifndef FA2_SM100_H_
 #define FA2_SM100_H_
@@ -24,7 +30,7 @@
 extern "C" {
 #endif
 
-#define FA2_SM100_ABI_VERSION 3
+#define FA2_SM100_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define FA2_API __attribute__((visibility("default")))
@@ -60,6 +66,9 @@ enum Fa2Status {
   FA2_ERR_SCRATCH_LIMIT = 14 /* fa2_fwd_sm100_noalloc: the split-KV scratch this call needs is
                                 larger than FA2_NOALLOC_SCRATCH_BYTES */
 };
+/* Device-side reports in err_flag: the kernel writes FA2_ERR_TIMEOUT (a bounded wait expired)
+ * or FA2_ERR_SHAPE (a variable-length sequence longer than seqlen_q / seqlen_kv, or negative)
+ * into a zero word; the first report wins. */
 
 /* Size of the library-owned device scratch behind fa2_fwd_sm100_noalloc (32 MiB). */
 #define FA2_NOALLOC_SCRATCH_BYTES (32ll << 20)
@@ -80,11 +89,10 @@ typedef struct Fa2FwdParams {
   int32_t seqlen_kv;
   int32_t head_dim;  /* 64 or 128 */
   int32_t dtype;     /* Fa2DType */
-  int32_t causal;    /* causal mask, aligned as causal_align says */
+  int32_t causal;    /* causal mask, aligned as causal_align says (per sequence when variable-length) */
   int32_t pack_gqa;  /* 1: a GQA group's query heads share one 128-row tile */
   float qk_scale;    /* sm_scale * log2(e), > 0 (fa2/kernel.py:240-244) */
-  int32_t* err_flag; /* optional device int32; a kernel that gives up on a wait ORs
-                        FA2_ERR_TIMEOUT into it. NULL: no report. */
+  int32_t* err_flag; /* optional device int32 for device-side reports (see above). NULL: none. */
   int64_t timeout_cycles; /* per-wait limit in SM clocks; <= 0 selects the default (~1 s) */
   const int32_t* gate;     /* optional device int32 start gate: the kernel issues its first
                               load only once *gate != 0 (set by an upstream kernel or a copy
@@ -98,6 +106,12 @@ typedef struct Fa2FwdParams {
   void* workspace;         /* device scratch for num_splits > 1 (fp32 partial O + row
                               log-sum-exp), at least fa2_fwd_sm100_workspace_bytes() bytes */
   int64_t workspace_bytes;
+  const int32_t* cu_seqlens_q;  /* variable-length batch: device int32 [batch + 1], the prefix sums
+                                   of the query lengths (cu_seqlens_q[0] == 0). NULL: every
+                                   sequence has seqlen_q queries and seqlen_kv keys. */
+  const int32_t* cu_seqlens_kv; /* the same for the keys; set together with cu_seqlens_q */
+  int32_t total_q;              /* variable-length batch: rows of q and o on the token axis */
+  int32_t total_kv;             /* variable-length batch: rows of k and v on the token axis */
 } Fa2FwdParams;
 
 /* Host-only validation of `p` (no CUDA calls). Replaces the asserts and ValueErrors of

@@ -67,6 +67,30 @@ def naive_attention(q, k, v, causal=True, sm_scale=None, dtype=None, causal_alig
     return out
 
 
+def naive_attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, causal=True, sm_scale=None, dtype=None,
+                           causal_align="top_left"):
+    """Variable-length batch (an extension; the reference has no such mode): sequences packed
+    along one token axis, q [total_q, H_q, D], k/v [total_k, H_kv, D], sequence b owning rows
+    cu_seqlens[b]:cu_seqlens[b + 1]. Each sequence is naive_attention on its own ([1, H, n, D]),
+    with the causal mask per sequence; a query that sees no key (no keys, or bottom-right rows
+    before the first key) is defined as zeros, as the kernel writes them."""
+    dtype = dtype or q.dtype
+    out = torch.zeros(q.shape, dtype=dtype, device=q.device)
+    cq = [int(x) for x in cu_seqlens_q.tolist()]
+    ck = [int(x) for x in cu_seqlens_k.tolist()]
+    for b in range(len(cq) - 1):
+        nq, nk = cq[b + 1] - cq[b], ck[b + 1] - ck[b]
+        if nq == 0 or nk == 0:
+            continue
+        qs = q[cq[b]:cq[b + 1]].transpose(0, 1).unsqueeze(0)   # [1, H_q, nq, D]
+        ks = k[ck[b]:ck[b + 1]].transpose(0, 1).unsqueeze(0)
+        vs = v[ck[b]:ck[b + 1]].transpose(0, 1).unsqueeze(0)
+        o = naive_attention(qs, ks, vs, causal=causal, sm_scale=sm_scale, dtype=dtype, causal_align=causal_align)
+        o = torch.nan_to_num(o, nan=0.0)                        # rows with no visible key
+        out[cq[b]:cq[b + 1]] = o[0].transpose(0, 1)
+    return out
+
+
 def _tile_walk(n_kv, row_lo, row_hi, causal, block_n):
     """K/V column ranges a Q tile of rows [row_lo, row_hi) visits, with a mask flag:
     stage 1 = whole block_n tiles left of row_lo (no mask), stage 2 = the diagonal band up

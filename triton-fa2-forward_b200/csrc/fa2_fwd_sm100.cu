@@ -302,6 +302,14 @@ struct KArgs {
   // top-left alignment (N_q == N_kv); N_kv - N_q aligns the last query with the last key
   // (bottom-right, for chunked prefill and decode with N_q <= N_kv).
   int causal_off;
+  int bottom_right;                     // variable-length: causal_off is N_kv - N_q per sequence
+  // Variable-length batch: sequence b owns Q positions [cu_q[b], cu_q[b + 1]) and K/V positions
+  // [cu_kv[b], cu_kv[b + 1]) of one packed token axis (the tensor maps' b extent is 1); n_q and
+  // n_kv are the largest lengths. nullptr: fixed lengths n_q / n_kv, batch on the maps' b axis.
+  const int* cu_q;
+  const int* cu_kv;
+  void* o;                              // output base and element strides (h, n): used for the
+  int64_t oh, on;                       // rows of a variable-length sequence's last O box
   int pack_shift;                       // pack == 1 << pack_shift (pack divides 128)
   FastDiv div_xblocks, div_hblocks, div_group;
   float qk_scale;
@@ -339,13 +347,18 @@ __host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, 
 
 // One work unit: packed Q rows [row0, row0 + 256) of batch b, q heads from hq0 (K/V head hkv),
 // against K/V tiles [j0, j0 + J) (in dual mode the second Q-tile slot walks [j0b, j0b + J)).
+// q0 / kv0: first Q / K/V position of the unit's sequence on the tensor maps' n axis, tb its
+// b coordinate (0 for a variable-length batch); n_q / n_kv / coff: the sequence's lengths and
+// causal shift.
 struct Unit {
   int x, b, hq0, hkv, row0, j0, j0b, J;
+  int q0, kv0, tb, n_q, n_kv, coff;
 };
 
-// Unit n of this CTA; false when the CTA has no n-th unit. J == 0: the unit is empty (a split
-// past its row block's causal band).
-template <bool CAUSAL>
+// Unit slot n of this CTA; false when the CTA has no n-th slot. J == 0: the unit is empty (a
+// split past its row block's causal band, or a row block past a shorter sequence's end).
+// VARLEN: the variable-length build (a.cu_q != nullptr exactly then).
+template <bool CAUSAL, bool VARLEN>
 __device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
   int mb, z = 0;
   if (a.persistent) {
@@ -367,9 +380,36 @@ __device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
   u.hkv = static_cast<int>(a.div_group.div(static_cast<uint32_t>(u.hq0)));
   static_assert(Q_TILES * BM == 256 && BN == 128, "cta_kv_tiles assumes 256-row CTAs, 128-row K/V tiles");
   u.row0 = mb * (Q_TILES * BM);
-  const int J_cta = cta_kv_tiles<CAUSAL>(mb, a.n_q, a.n_kv, a.pack_shift, a.causal_off);
   u.j0 = 0;
   u.j0b = 0;
+  if constexpr (VARLEN) {
+    u.q0 = __ldg(a.cu_q + u.b);
+    u.kv0 = __ldg(a.cu_kv + u.b);
+    u.n_q = __ldg(a.cu_q + u.b + 1) - u.q0;
+    u.n_kv = __ldg(a.cu_kv + u.b + 1) - u.kv0;
+    u.tb = 0;
+    u.coff = a.bottom_right ? u.n_kv - u.n_q : 0;
+    if (u.n_q < 0 || u.n_kv < 0 || u.n_q > a.n_q || u.n_kv > a.n_kv) {
+      // Lengths the launch was not sized for: reported, and the unit is left out.
+      if (a.err != nullptr) atomicCAS(a.err, 0, FA2_ERR_SHAPE);
+      u.J = 0;
+      return true;
+    }
+    if (u.row0 >= (u.n_q << a.pack_shift)) {  // past this sequence's last row
+      u.J = 0;
+      return true;
+    }
+  } else {
+    u.q0 = 0;
+    u.kv0 = 0;
+    u.tb = u.b;
+    u.n_q = a.n_q;
+    u.n_kv = a.n_kv;
+    u.coff = a.causal_off;
+  }
+  // At least one K/V tile: rows that see no key at all (a sequence without keys, or
+  // bottom-right rows before the first key) then get exact zeros from a fully masked tile.
+  const int J_cta = max(1, cta_kv_tiles<CAUSAL>(mb, u.n_q, u.n_kv, a.pack_shift, u.coff));
   u.J = J_cta;
   if (a.num_splits > 1) {
     if (a.dual) {
@@ -382,6 +422,17 @@ __device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
     }
   }
   return true;
+}
+
+// The next non-empty unit after slot `slot` (which it advances past the unit); false when the
+// CTA has no more. Every role walks the same slots, so all of them see the same units.
+template <bool CAUSAL, bool VARLEN>
+__device__ __forceinline__ bool next_unit(const KArgs& a, int& slot, Unit& u) {
+  while (get_unit<CAUSAL, VARLEN>(a, slot, u)) {
+    ++slot;
+    if (u.J > 0) return true;
+  }
+  return false;
 }
 
 // ---------------------------------------------------------------- softmax helpers
@@ -485,8 +536,9 @@ __device__ __forceinline__ void rescale_o_cols(uint32_t tO, float alpha) {
 }
 
 // ------------------------------------------------------------------------ kernel
-// SPLIT: the split-KV build (num_splits > 1); the host launches it exactly then.
-template <int D, bool CAUSAL, bool BF16, bool SPLIT>
+// SPLIT: the split-KV build (num_splits > 1); VARLEN: the variable-length build
+// (cu_seqlens given). The host launches each exactly then; never both.
+template <int D, bool CAUSAL, bool BF16, bool SPLIT, bool VARLEN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
@@ -504,7 +556,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
   const bool dual = (a.dual != 0);
   {
     Unit u0;
-    if (!get_unit<CAUSAL>(a, 0, u0) || u0.J <= 0) return;  // nothing to do (uniform, before any sync)
+    int s0 = 0;
+    if (!next_unit<CAUSAL, VARLEN>(a, s0, u0)) return;  // nothing to do (uniform, before any sync)
   }
 
   // MMA-issuing threads: every K/V slot is released, and the teardown barrier arrived at, by each.
@@ -564,16 +617,17 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
         for (int c = 0; c < C::CHUNKS; ++c) {
           tma_load_4d(sbase + C::OFF_Q + t * C::TILE_BYTES + c * C::CHUNK_BYTES, &tmQ, bar(C::B_Q + t),
-                      c * 64, h, pos, u.b, pol_q);
+                      c * 64, h, u.q0 + pos, u.tb, pol_q);
         }
         if (t == 0) ++q_loads0; else ++q_loads1;
       };
       // Optional start gate: no load is issued before *gate != 0 (bounded like every wait).
       if (a.gate != nullptr) ok = flag_wait(a.gate, a.timeout, a.err);
       int i = 0;  // K/V tiles issued into the ring, over all units
+      int slot = 0;
       for (int n = 0; ok; ++n) {
         Unit u;
-        if (!get_unit<CAUSAL>(a, n, u)) break;
+        if (!next_unit<CAUSAL, VARLEN>(a, slot, u)) break;
         // Q_t's buffer is free once the last QK GEMM of tile t of the previous unit retired.
         if (n > 0 && !mbar_wait(bar(C::B_Q_EMPTY + 0), static_cast<uint32_t>(n - 1) & 1u, a.timeout, a.err)) {
           ok = false;
@@ -614,7 +668,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
           for (int c = 0; c < C::CHUNKS; ++c) {
             tma_load_4d(sbase + C::OFF_KV + st * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
-                        bar(C::B_KV_FULL + st), c * 64, kv_tile * BN, u.hkv, u.b, pol_kv);
+                        bar(C::B_KV_FULL + st), c * 64, u.kv0 + kv_tile * BN, u.hkv, u.tb, pol_kv);
           }
           ++i;
           if (k == 0 && !dual) {
@@ -692,7 +746,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         return mwait(C::B_KV_FULL + i % C::STAGES, static_cast<uint32_t>(i / C::STAGES) & 1u);
       };
       Unit u;
-      get_unit<CAUSAL>(a, 0, u);
+      int slot = 0;
+      next_unit<CAUSAL, VARLEN>(a, slot, u);
       if (dual) {
         // One unit. Each K/V tile feeds one Q tile; ci walks the ring in the loader's order.
         int ci = 0;
@@ -749,7 +804,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           int n = 0, i = 0, g = 0;  // unit, ring position of its K_0, steps of the units before
           while (true) {
             Unit nx;
-            const bool has_next = get_unit<CAUSAL>(a, n + 1, nx);
+            int slot_next = slot;
+            const bool has_next = next_unit<CAUSAL, VARLEN>(a, slot_next, nx);
             const uint32_t qph_next = static_cast<uint32_t>(n + 1) & 1u;
             for (int j = 0; j < u.J; ++j) {
               const bool last = (j + 1 == u.J);
@@ -775,6 +831,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             g += u.J;
             ++n;
             u = nx;
+            slot = slot_next;
           }
         } while (false);
       } else {
@@ -795,7 +852,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           int n = 0, i = 0, g = 0;  // unit, ring position of its K_0, steps of the units before
           while (true) {
             Unit nx;
-            const bool has_next = get_unit<CAUSAL>(a, n + 1, nx);
+            int slot_next = slot;
+            const bool has_next = next_unit<CAUSAL, VARLEN>(a, slot_next, nx);
             const uint32_t qph_next = static_cast<uint32_t>(n + 1) & 1u;
             for (int j = 0; j < u.J; ++j) {
               const bool last = (j + 1 == u.J);
@@ -832,6 +890,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             g += u.J;
             ++n;
             u = nx;
+            slot = slot_next;
           }
         } while (false);
       }
@@ -900,7 +959,8 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       if constexpr (FA2_SEQ_EXP != 0) mbar_arrive(bar(C::B_SEQ + t * 4 + q));
     };
     Unit u;
-    bool have = get_unit<CAUSAL>(a, 0, u);
+    int slot = 0;
+    bool have = next_unit<CAUSAL, VARLEN>(a, slot, u);
     for (int n = 0; ok && have; ++n) {
       const int J = u.J;
       const int tile_row0 = u.row0 + (dual ? 0 : t * BM);  // dual: both tiles hold Q tile 0's rows
@@ -915,11 +975,11 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
         tc_fence_after();
         const int col0 = (kv_base + j) * BN;
-        const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0 + a.causal_off);
-        const bool need_pad = (col0 + BN > a.n_kv);
+        const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0 + u.coff);
+        const bool need_pad = (col0 + BN > u.n_kv);
         const bool masked = need_causal || need_pad;  // uniform over the tile's warps
-        int lim = a.n_kv - 1 - col0;                  // last visible column of this tile, relative
-        if (CAUSAL) lim = min(lim, pos + a.causal_off - col0);
+        int lim = u.n_kv - 1 - col0;                  // last visible column of this tile, relative
+        if (CAUSAL) lim = min(lim, pos + u.coff - col0);
 
         // This warp's scores of the row in one batch of loads and a single wait.
         uint32_t s[NCH][32];
@@ -1070,7 +1130,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       g += J;
       // The next unit, decoded while PV(t, J - 1) runs.
       Unit nu;
-      have = get_unit<CAUSAL>(a, n + 1, nu);
+      have = next_unit<CAUSAL, VARLEN>(a, slot, nu);
 
       // -------------------------------------------------------------- epilogue
       {
@@ -1126,11 +1186,22 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           // for the slot to have been read before it is rewritten (the next chunk's conversion
           // overlaps the read).
           constexpr int ECH = C::EPI_COLS / 64;  // 64-column chunks
-          const float inv_l = 1.0f / l_row;
+          // A row that saw no key at all (a variable-length sequence without keys, bottom-right
+          // rows before the first key) has l == 0 and gets zeros.
+          const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
           const uint64_t inv2 = f2_pack(inv_l, inv_l);
           const int R0 = tile_row0 + q * 32;  // first row of this warp
           const int pos0 = R0 >> a.pack_shift;
           const int h0 = u.hq0 + (R0 & (a.pack - 1));
+          // The warp's O box covers 32 / min(PACK, 32) positions. In a variable-length batch a box
+          // that reaches past its sequence's last position would overwrite the next sequence's
+          // rows (the tensor map only clips at the end of the token axis), so such a box is
+          // written row by row from registers instead.
+          const bool rowwise = VARLEN && pos0 + (32 >> min(a.pack_shift, 5)) > u.n_q;
+          const int my_pos = (R0 + lane) >> a.pack_shift;
+          uint16_t* my_row = static_cast<uint16_t*>(a.o) + static_cast<int64_t>(u.q0 + my_pos) * a.on +
+                             static_cast<int64_t>(u.hq0 + ((R0 + lane) & (a.pack - 1))) * a.oh + epi_c0;
+          const bool my_valid = my_pos < u.n_q;
 #pragma unroll
           for (int ch = 0; ch < ECH; ++ch) {
             const uint32_t slot = so + (FA2_STG_FULL ? ch * C::STG_SLOT_BYTES : 0);
@@ -1150,17 +1221,21 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 f2_unpack(f2_mul(f2_pack(__uint_as_float(src[e]), __uint_as_float(src[e + 1])), inv2), x0, x1);
                 w4[i] = cvt_pack2<BF16>(x0, x1);
               }
-              st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
-                           w4[0], w4[1], w4[2], w4[3]);
+              if (rowwise) {
+                if (my_valid) *reinterpret_cast<uint4*>(my_row + ch * 64 + v * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+              } else {
+                st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
+                             w4[0], w4[1], w4[2], w4[3]);
+              }
             }
-            if (!FA2_STG_FULL || ch == ECH - 1) {
+            if (!rowwise && (!FA2_STG_FULL || ch == ECH - 1)) {
               fence_proxy_async_smem();
               __syncwarp();
-              if (lane == 0 && pos0 < a.n_q) {
+              if (lane == 0 && pos0 < u.n_q) {
 #pragma unroll
                 for (int c2 = (FA2_STG_FULL ? 0 : ch); c2 <= ch; ++c2) {
-                  tma_store_4d(&tmO, so + (FA2_STG_FULL ? c2 * C::STG_SLOT_BYTES : 0), epi_c0 + c2 * 64, h0, pos0,
-                               u.b);
+                  tma_store_4d(&tmO, so + (FA2_STG_FULL ? c2 * C::STG_SLOT_BYTES : 0), epi_c0 + c2 * 64, h0,
+                               u.q0 + pos0, u.tb);
                 }
                 bulk_commit();
               }
@@ -1176,7 +1251,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     reg_dealloc<regs_other<D>()>();
   }
 
-  if (!ok && a.err != nullptr) atomicOr(a.err, FA2_ERR_TIMEOUT);
+  if (!ok && a.err != nullptr) atomicCAS(a.err, 0, FA2_ERR_TIMEOUT);  // the first report wins
 
   tc_fence_before();
   __syncthreads();
@@ -1334,15 +1409,19 @@ SplitPlan plan_splits(const Fa2FwdParams* p) {
 template <int D, bool CAUSAL, bool BF16>
 int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   const bool split = plan_splits(p).num_splits > 1;
-  auto kern = split ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, true> : fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false>;
+  const bool is_varlen = p->cu_seqlens_q != nullptr;  // never together with split (validated)
+  auto kern = split ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, true, false>
+                    : (is_varlen ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false, true>
+                                 : fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false, false>);
   const int smem_alloc = split ? Cfg<D, true>::SMEM_ALLOC : Cfg<D, false>::SMEM_ALLOC;
-  static bool attr_done[2][kMaxDevices] = {};
+  const int variant = split ? 1 : (is_varlen ? 2 : 0);
+  static bool attr_done[3][kMaxDevices] = {};
   if (device < 0 || device >= kMaxDevices) return FA2_ERR_DEVICE;
-  if (!attr_done[split][device]) {
+  if (!attr_done[variant][device]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_alloc) != cudaSuccess) {
       return FA2_ERR_LAUNCH;
     }
-    attr_done[split][device] = true;
+    attr_done[variant][device] = true;
   }
   const int group = p->heads_q / p->heads_kv;
   const int pack = p->pack_gqa ? group : 1;
@@ -1350,7 +1429,9 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   // Q / O: dims (d, h, n, b). A box row is a (position, head) pair, heads fastest, so a
   // packed tile is exactly rows r -> (position r / PACK, head r % PACK).
   CUtensorMap tmQ, tmK, tmV, tmO;
-  const int64_t qdims[4] = {D, p->heads_q, p->seqlen_q, p->batch};
+  // Variable-length batches: one packed token axis (b extent 1) of total_q / total_kv rows.
+  const bool varlen = p->cu_seqlens_q != nullptr;
+  const int64_t qdims[4] = {D, p->heads_q, varlen ? p->total_q : p->seqlen_q, varlen ? 1 : p->batch};
   const int64_t qstr[4] = {1, p->q_stride[1], p->q_stride[2], p->q_stride[0]};
   const int64_t ostr[4] = {1, p->o_stride[1], p->o_stride[2], p->o_stride[0]};
   const uint32_t gh_q = static_cast<uint32_t>(pack);           // heads per 128-row Q box
@@ -1358,7 +1439,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   const uint32_t gh_o = static_cast<uint32_t>(pack < 32 ? pack : 32);  // 32-row O box per warp
   const uint32_t obox[4] = {64, gh_o, 32u / gh_o, 1};
   // K / V: dims (d, n, h, b), 128-row boxes of one head.
-  const int64_t kdims[4] = {D, p->seqlen_kv, p->heads_kv, p->batch};
+  const int64_t kdims[4] = {D, varlen ? p->total_kv : p->seqlen_kv, p->heads_kv, varlen ? 1 : p->batch};
   const int64_t kstr[4] = {1, p->k_stride[2], p->k_stride[1], p->k_stride[0]};
   const int64_t vstr[4] = {1, p->v_stride[2], p->v_stride[1], p->v_stride[0]};
   const uint32_t kvbox[4] = {64, static_cast<uint32_t>(fa2::BN), 1, 1};
@@ -1376,7 +1457,13 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.pack_shift = 0;
   while ((1 << ka.pack_shift) < pack) ++ka.pack_shift;  // pack divides 128: a power of two
   ka.hblocks = p->heads_q / pack;
-  ka.causal_off = (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT) ? p->seqlen_kv - p->seqlen_q : 0;
+  ka.bottom_right = (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT) ? 1 : 0;
+  ka.causal_off = (ka.bottom_right && !varlen) ? p->seqlen_kv - p->seqlen_q : 0;
+  ka.cu_q = p->cu_seqlens_q;
+  ka.cu_kv = p->cu_seqlens_kv;
+  ka.o = p->o;
+  ka.oh = p->o_stride[1];
+  ka.on = p->o_stride[2];
   ka.qk_scale = p->qk_scale;
   ka.err = p->err_flag;
   ka.gate = p->gate;
@@ -1514,8 +1601,16 @@ int check_core(const Fa2FwdParams* p) {
   if (p == nullptr || p->q == nullptr || p->k == nullptr || p->v == nullptr || p->o == nullptr) return FA2_ERR_NULL;
   if (p->batch < 1 || p->heads_q < 1 || p->heads_kv < 1 || p->seqlen_q < 0 || p->seqlen_kv < 1) return FA2_ERR_SHAPE;
   if (p->causal_align != FA2_CAUSAL_TOP_LEFT && p->causal_align != FA2_CAUSAL_BOTTOM_RIGHT) return FA2_ERR_SHAPE;
-  if (p->causal && p->causal_align == FA2_CAUSAL_TOP_LEFT && p->seqlen_q != p->seqlen_kv) return FA2_ERR_SHAPE;
-  if (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT && p->seqlen_q > p->seqlen_kv) return FA2_ERR_SHAPE;
+  const bool varlen = p->cu_seqlens_q != nullptr || p->cu_seqlens_kv != nullptr;
+  if (varlen) {
+    // Per-sequence lengths live on the device; the causal mask applies per sequence, with its
+    // alignment, whatever the lengths. Split-KV is not offered for variable-length batches.
+    if (p->cu_seqlens_q == nullptr || p->cu_seqlens_kv == nullptr) return FA2_ERR_NULL;
+    if (p->total_q < 0 || p->total_kv < 1 || p->num_splits > 1) return FA2_ERR_SHAPE;
+  } else {
+    if (p->causal && p->causal_align == FA2_CAUSAL_TOP_LEFT && p->seqlen_q != p->seqlen_kv) return FA2_ERR_SHAPE;
+    if (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT && p->seqlen_q > p->seqlen_kv) return FA2_ERR_SHAPE;
+  }
   if (p->dtype != FA2_DTYPE_FP16 && p->dtype != FA2_DTYPE_BF16) return FA2_ERR_DTYPE;
   if (p->head_dim != 64 && p->head_dim != 128) return FA2_ERR_HEAD_DIM;
   if (p->heads_q % p->heads_kv != 0) return FA2_ERR_GQA;
@@ -1526,8 +1621,8 @@ int check_core(const Fa2FwdParams* p) {
   const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
   if ((rows + 255) / 256 > 65535) return FA2_ERR_SHAPE;
   if (static_cast<int64_t>(p->batch) * (p->heads_q / pack) > 0x7fffffffLL) return FA2_ERR_SHAPE;
-  const int64_t qext[4] = {p->batch, p->heads_q, p->seqlen_q, p->head_dim};
-  const int64_t kext[4] = {p->batch, p->heads_kv, p->seqlen_kv, p->head_dim};
+  const int64_t qext[4] = {varlen ? 1 : p->batch, p->heads_q, varlen ? p->total_q : p->seqlen_q, p->head_dim};
+  const int64_t kext[4] = {varlen ? 1 : p->batch, p->heads_kv, varlen ? p->total_kv : p->seqlen_kv, p->head_dim};
   if (!layout_ok(p->q_stride, qext) || !layout_ok(p->o_stride, qext) || !layout_ok(p->k_stride, kext) ||
       !layout_ok(p->v_stride, kext)) {
     return FA2_ERR_LAYOUT;
@@ -1560,7 +1655,7 @@ int64_t fa2_fwd_sm100_workspace_bytes(const Fa2FwdParams* p) {
 int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream) {
   const int rc = fa2_fwd_sm100_check(p);
   if (rc != FA2_OK) return rc;
-  if (p->seqlen_q == 0) return FA2_OK;
+  if (p->seqlen_q == 0 || (p->cu_seqlens_q != nullptr && p->total_q == 0)) return FA2_OK;
   int dev = -1, major = 0, minor = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FA2_ERR_DEVICE;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||

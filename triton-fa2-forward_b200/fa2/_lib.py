@@ -10,7 +10,7 @@ import os
 LIB_NAME = "libfa2_sm100.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 FA2_DTYPE_FP16 = 0
 FA2_DTYPE_BF16 = 1
@@ -77,6 +77,10 @@ class Fa2FwdParams(ctypes.Structure):
         ("causal_align", ctypes.c_int32),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_int64),
+        ("cu_seqlens_q", ctypes.c_void_p),
+        ("cu_seqlens_kv", ctypes.c_void_p),
+        ("total_q", ctypes.c_int32),
+        ("total_kv", ctypes.c_int32),
     ]
 
 
@@ -146,7 +150,8 @@ def config(head_dim):
 def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stride,
                 batch, heads_q, heads_kv, seqlen_q, seqlen_kv, head_dim, dtype, causal,
                 pack_gqa, qk_scale, err_flag=0, timeout_cycles=0, gate=0, num_splits=1,
-                workspace=0, workspace_bytes=0, causal_align=FA2_CAUSAL_TOP_LEFT):
+                workspace=0, workspace_bytes=0, causal_align=FA2_CAUSAL_TOP_LEFT,
+                cu_seqlens_q=0, cu_seqlens_kv=0, total_q=0, total_kv=0):
     p = Fa2FwdParams()
     p.q, p.k, p.v, p.o = q_ptr, k_ptr, v_ptr, o_ptr
     p.q_stride[:] = list(q_stride)
@@ -164,6 +169,9 @@ def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stri
     p.causal_align = int(causal_align)
     p.workspace = workspace or None
     p.workspace_bytes = int(workspace_bytes)
+    p.cu_seqlens_q = cu_seqlens_q or None
+    p.cu_seqlens_kv = cu_seqlens_kv or None
+    p.total_q, p.total_kv = int(total_q), int(total_kv)
     return p
 
 

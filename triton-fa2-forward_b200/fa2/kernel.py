@@ -22,6 +22,10 @@ Differences from the reference that do not change results:
   * head_dim 16 and 32 run the 64 kernel on zero-padded copies (extra zero columns add
     nothing to QK^T and produce zero output columns that are dropped).
 
+Also (no counterpart in the reference, whose README lists variable-length batches out of scope):
+    attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal=True, ...)
+with q [total_q, H_q, D], k/v [total_k, H_kv, D] packed along one token axis.
+
 Extensions (keyword arguments the reference does not have; their defaults keep its behaviour):
   * causal_align="bottom_right": the causal mask lines the last query up with the last key
     (query i sees keys j <= i + N_kv - N_q), for chunked prefill and decode with N_q <= N_kv.
@@ -245,3 +249,81 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
         out.copy_(op[..., :D])
         return out
     return _run(q, k, v, out, causal, pack, qk_scale, num_splits, align=align)
+
+
+def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal=True,
+                     sm_scale=None, pack_gqa=None, causal_align="top_left"):
+    """Attention over a batch of sequences of different lengths packed along one token axis
+    (the layout of flash_attn_varlen_func). An extension: the reference has no such entry point.
+
+    q: [total_q, H_q, D]; k, v: [total_k, H_kv, D]; cu_seqlens_q / cu_seqlens_k: int32 CUDA
+    tensors [B + 1] of prefix sums (sequence b owns q rows cu_seqlens_q[b]:cu_seqlens_q[b+1]);
+    max_seqlen_q / max_seqlen_k: upper bounds of the lengths (a longer sequence is reported as a
+    device error, see check_device_errors). Each sequence is attended on its own, with the causal
+    mask per sequence ("top_left": query i sees keys j <= i; "bottom_right": j <= i + n_k - n_q).
+    A query that sees no key gets zeros. Returns [total_q, H_q, D]; asynchronous like attention().
+    """
+    assert q.dim() == k.dim() == v.dim() == 3
+    total_q, H_q, D = q.shape
+    total_k, H_kv, Dk = k.shape
+    assert v.shape == k.shape and Dk == D
+    assert q.dtype == k.dtype == v.dtype and q.dtype in (torch.float16, torch.bfloat16)
+    assert H_q % H_kv == 0, "GQA needs H_q divisible by H_kv"
+    assert D in (16, 32, 64, 128), "head_dim must be a power of two in [16, 128]"
+    assert causal_align in CAUSAL_ALIGNS, f"causal_align must be one of {sorted(CAUSAL_ALIGNS)}"
+    assert cu_seqlens_q.dtype == torch.int32 and cu_seqlens_k.dtype == torch.int32
+    assert cu_seqlens_q.dim() == 1 and cu_seqlens_q.shape == cu_seqlens_k.shape and cu_seqlens_q.numel() >= 2
+    if not (q.is_cuda and k.is_cuda and v.is_cuda and cu_seqlens_q.is_cuda and cu_seqlens_k.is_cuda):
+        raise RuntimeError("fa2.kernel.attention_varlen runs only on an sm_100 CUDA device (no CPU path)")
+    B = cu_seqlens_q.numel() - 1
+    group = H_q // H_kv
+    if pack_gqa is None:
+        pack_gqa = group > 1 and KERNEL_BLOCK_M % group == 0
+    elif pack_gqa and KERNEL_BLOCK_M % group:
+        raise ValueError(f"pack_gqa needs BLOCK_M ({KERNEL_BLOCK_M}) to be a multiple of the GQA group ({group})")
+    pack = bool(pack_gqa) and group > 1
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if not sm_scale > 0:
+        raise ValueError(f"sm_scale must be positive (the row max is scaled after it is taken), got {sm_scale}")
+    out = torch.empty_like(q)
+    if total_q == 0 or max_seqlen_q == 0:
+        return out
+    if total_k == 0 or max_seqlen_k == 0:
+        return out.zero_()  # no sequence has a key: every query sees none
+    if D < 64:
+        pad = (0, 64 - D)
+        qp, kp, vp = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
+        op = attention_varlen(qp, kp, vp, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal,
+                              sm_scale, pack_gqa, causal_align)
+        out.copy_(op[..., :D])
+        return out
+    cq, ck = cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous()
+
+    def launch(qq, kk, vv, oo, pk):
+        err = _err_word(qq.device)
+        st = lambda t: (0, int(t.stride(1)), int(t.stride(0)), int(t.stride(2)))  # noqa: E731
+        p = _lib.make_params(
+            qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), oo.data_ptr(), st(qq), st(kk), st(vv), st(oo),
+            B, H_q, H_kv, int(max_seqlen_q), int(max_seqlen_k), D,
+            _lib.FA2_DTYPE_BF16 if qq.dtype == torch.bfloat16 else _lib.FA2_DTYPE_FP16,
+            causal, pk, sm_scale * LOG2E, err.data_ptr(), 0, causal_align=CAUSAL_ALIGNS[causal_align],
+            cu_seqlens_q=cq.data_ptr(), cu_seqlens_kv=ck.data_ptr(), total_q=total_q, total_kv=total_k)
+        return _lib.launch(p, torch.cuda.current_stream(qq.device).cuda_stream)
+
+    with torch.cuda.device(q.device):
+        rc = launch(q, k, v, out, pack)
+        if rc == _lib.FA2_ERR_TMA_ENCODE and pack:
+            pack = False
+            rc = launch(q, k, v, out, pack)
+        if rc in (_lib.FA2_ERR_LAYOUT, _lib.FA2_ERR_TMA_ENCODE):
+            qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+            oc = torch.empty_like(qc)
+            rc = launch(qc, kc, vc, oc, pack)
+            if rc == _lib.FA2_OK:
+                out.copy_(oc)
+        if rc != _lib.FA2_OK:
+            raise _lib.Fa2Error(rc, _lib.strerror(rc))
+        if _sync_check_enabled():
+            check_device_errors(q.device)
+    return out
