@@ -36,6 +36,8 @@ Every variant computes the full attention (no work is skipped); they differ only
   row_split_2    two softmax warps per row quadrant, 64 scores each, exchanging the row max and
                  row sum through TMEM (FA2_ROW_SPLIT=2: 20 warps, setmaxnreg 104/64) instead of
                  one warp taking all 128 scores (12 warps, 200/104)
+  row_major_noncausal   without a causal mask, the persistent CTAs walk the units row block by
+                 row block (FA2_HEAD_MAJOR=0) instead of (batch, head) slice by slice
   seq_exp        the two softmax warps of a lane quadrant take turns on the exponential phase of
                  a step (FA2_SEQ_EXP=1, a bounded mbarrier hand-shake) instead of running freely
   ffma_pass      s * qk_scale - m for the whole row in one FMA pass before the exponentials
@@ -98,6 +100,7 @@ COMPILED = {
     "d64_regs_208": ["-DFA2_REGS_SOFTMAX_D64=208"],
     "fp16_poly_deg3": ["-DFA2_POLY_DEG_FP16=3", "-DFA2_EMU_MASK_D64=0x8080u"],
     "seq_exp": ["-DFA2_SEQ_EXP=1"],
+    "row_major_noncausal": ["-DFA2_HEAD_MAJOR=0"],
     "ffma_pass": ["-DFA2_FFMA_PASS=1"],
     "seq_exp_ffma_pass": ["-DFA2_SEQ_EXP=1", "-DFA2_FFMA_PASS=1"],
 }

@@ -84,7 +84,7 @@ constexpr int TMEM_COLS = 512;
 #define FA2_REGS_SOFTMAX_D128 200
 #endif
 #ifndef FA2_REGS_SOFTMAX_D64
-#define FA2_REGS_SOFTMAX_D64 200
+#define FA2_REGS_SOFTMAX_D64 192
 #endif
 // Columns per tcgen05.ld when a softmax warp loads its scores (32, 64 or 128), per head dim.
 // Measured: one 128-column load at D = 64 fp16 gave +2.8%, +3.6% and -0.3% on three boxes (bf16
@@ -179,6 +179,11 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #endif
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
+#endif
+#ifndef FA2_HEAD_MAJOR
+// 1: without a causal mask the persistent CTAs walk the units (batch, head) slice by slice;
+// 0: row block by row block, as with a causal mask (every head's K/V in flight at once).
+#define FA2_HEAD_MAJOR 1
 #endif
 #ifndef FA2_SEQ_EXP
 // 1: the two softmax warps of a lane quadrant (tile 0 and tile 1, on the same SMSP) take turns
@@ -311,7 +316,7 @@ struct KArgs {
   void* o;                              // output base and element strides (h, n): used for the
   int64_t oh, on;                       // rows of a variable-length sequence's last O box
   int pack_shift;                       // pack == 1 << pack_shift (pack divides 128)
-  FastDiv div_xblocks, div_hblocks, div_group;
+  FastDiv div_xblocks, div_hblocks, div_group, div_mblocks;
   float qk_scale;
   int* err;
   const int* gate;
@@ -366,9 +371,19 @@ __device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
     const uint32_t G = gridDim.x, c = blockIdx.x, nn = static_cast<uint32_t>(n);
     const uint32_t idx = nn * G + ((nn & 1u) ? (G - 1u - c) : c);
     if (idx >= static_cast<uint32_t>(a.num_units)) return false;
-    const uint32_t mi = a.div_xblocks.div(idx);
-    u.x = static_cast<int>(idx - mi * a.div_xblocks.d);
-    mb = CAUSAL ? a.mblocks - 1 - static_cast<int>(mi) : static_cast<int>(mi);
+    if (CAUSAL || !FA2_HEAD_MAJOR) {
+      // Row-block major, heaviest causal block first: the CTAs of a round share a row block
+      // and span the (batch, head) slices, which keeps the longest units at the front.
+      const uint32_t mi = a.div_xblocks.div(idx);
+      u.x = static_cast<int>(idx - mi * a.div_xblocks.d);
+      mb = CAUSAL ? a.mblocks - 1 - static_cast<int>(mi) : static_cast<int>(mi);
+    } else {
+      // Without a causal mask every unit has the same length: slice major, so the CTAs of a
+      // round read the K/V of a few heads (it stays in L2) instead of one row block of every head.
+      const uint32_t xs = a.div_mblocks.div(idx);
+      u.x = static_cast<int>(xs);
+      mb = static_cast<int>(idx - xs * a.div_mblocks.d);
+    }
   } else {
     if (n > 0) return false;
     u.x = static_cast<int>(blockIdx.x);
@@ -1490,6 +1505,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.div_xblocks = fa2::make_fastdiv(static_cast<uint32_t>(xblocks));
   ka.div_hblocks = fa2::make_fastdiv(static_cast<uint32_t>(ka.hblocks));
   ka.div_group = fa2::make_fastdiv(static_cast<uint32_t>(group));
+  ka.div_mblocks = fa2::make_fastdiv(static_cast<uint32_t>(mblocks));
   ka.mblocks = static_cast<int>(mblocks);
   ka.persistent = (FA2_PERSISTENT && sp.num_splits <= 1 && units <= 0x7fffffffLL) ? 1 : 0;
   ka.num_units = ka.persistent ? static_cast<int>(units) : 0;

@@ -73,6 +73,10 @@ def kernel_summary(path, flops=None, peak_tflops=None):
             out.append("  warp stall reasons (cycles per issued instruction):")
             for n, v in stalls[:10]:
                 out.append(f"    {n:24s} {v:.3f}")
+        # local-memory (register spill) traffic, when the capture has it
+        for h in ("smsp__sass_inst_executed_op_local_ld.sum", "smsp__sass_inst_executed_op_local_st.sum"):
+            if h in col and r[col[h]] not in ("", "n/a"):
+                out.append(f"  {h:34s} {r[col[h]]}")
         if "dram__bytes_read.sum" in vals and "dram__bytes_write.sum" in vals:
             rd = vals["dram__bytes_read.sum"][0] * UNIT_SCALE.get(vals["dram__bytes_read.sum"][1], 1)
             wr = vals["dram__bytes_write.sum"][0] * UNIT_SCALE.get(vals["dram__bytes_write.sum"][1], 1)
