@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/*.pt from the reference implementation itself.
 
-Runs ONLY in the build container, where the reference (roy6n23/triton-fa2-forward) is
-mounted read-only at REFERENCE_ROOT; the committed .pt files are what the tests use on any
+Runs only where a checkout of the reference (roy6n23/triton-fa2-forward) is available; its
+root directory is the required argument. The committed .pt files are what the tests use on any
 box. For each case it stores the seeded inputs and
   * ref_naive     fa2.reference.naive_attention on fp64 copies of the inputs (the
                   reference tests' ground truth, tests/test_correctness.py:93), as fp32
@@ -12,7 +12,7 @@ box. For each case it stores the seeded inputs and
                   dtype; omitted for bf16 (the interpreter's bf16 dot is wrong,
                   reference tests/test_correctness.py:116-121)
 
-    python tests/golden/make_golden.py [REFERENCE_ROOT]
+    python tests/golden/make_golden.py REFERENCE_ROOT
 """
 
 import os
@@ -22,7 +22,9 @@ os.environ["TRITON_INTERPRET"] = "1"  # must precede the first triton import
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF_ROOT = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2 or not os.path.isdir(os.path.join(sys.argv[1], "fa2")):
+    sys.exit("usage: python tests/golden/make_golden.py REFERENCE_ROOT  (the directory holding the reference's fa2/)")
+REF_ROOT = sys.argv[1]
 
 sys.path.insert(0, REPO)
 import torch  # noqa: E402
