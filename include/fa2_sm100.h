@@ -20,6 +20,12 @@
  * flash_attn_varlen_func). Sequence b owns q rows [cu_seqlens_q[b], cu_seqlens_q[b + 1]) and
  * k/v rows [cu_seqlens_kv[b], cu_seqlens_kv[b + 1]); seqlen_q / seqlen_kv are the largest
  * lengths, and the (b, h, n, d) strides give the token axis as n (the b stride is unused).
+ *
+ * Paged K/V (block_table != NULL): k and v are caches of pages [num_pages, page_size, H_kv, D]
+ * (the layout of flash_attn_with_kvcache); sequence b's keys j live in page
+ * block_table[b * block_table_stride + j / page_size], row j % page_size, and seqlens_kv[b]
+ * says how many there are (at most seqlen_kv). The k/v strides are given as (page, h, row, d).
+ * q and o keep the fixed-length layout [B, H_q, N_q, D].
  */
 #ifndef FA2_SM100_H_
 #define FA2_SM100_H_
@@ -30,7 +36,7 @@
 extern "C" {
 #endif
 
-#define FA2_SM100_ABI_VERSION 4
+#define FA2_SM100_ABI_VERSION 5
 
 #if defined(__GNUC__)
 #define FA2_API __attribute__((visibility("default")))
@@ -67,8 +73,8 @@ enum Fa2Status {
                                 larger than FA2_NOALLOC_SCRATCH_BYTES */
 };
 /* Device-side reports in err_flag: the kernel writes FA2_ERR_TIMEOUT (a bounded wait expired)
- * or FA2_ERR_SHAPE (a variable-length sequence longer than seqlen_q / seqlen_kv, or negative)
- * into a zero word; the first report wins. */
+ * or FA2_ERR_SHAPE (a variable-length or paged sequence longer than seqlen_q / seqlen_kv, or
+ * negative) into a zero word; the first report wins. */
 
 /* Size of the library-owned device scratch behind fa2_fwd_sm100_noalloc (32 MiB). */
 #define FA2_NOALLOC_SCRATCH_BYTES (32ll << 20)
@@ -112,6 +118,13 @@ typedef struct Fa2FwdParams {
   const int32_t* cu_seqlens_kv; /* the same for the keys; set together with cu_seqlens_q */
   int32_t total_q;              /* variable-length batch: rows of q and o on the token axis */
   int32_t total_kv;             /* variable-length batch: rows of k and v on the token axis */
+  const int32_t* block_table;   /* paged K/V: device int32 [batch][block_table_stride] page indices.
+                                   NULL: k and v are contiguous [B, H_kv, N_kv, D] (or varlen). */
+  const int32_t* seqlens_kv;    /* paged K/V: device int32 [batch], keys of each sequence */
+  int32_t block_table_stride;   /* paged K/V: entries per sequence in block_table */
+  int32_t page_size;            /* paged K/V: keys per page, 16, 32, 64 or a multiple of 128 */
+  int32_t num_pages;            /* paged K/V: pages in k and v */
+  int32_t reserved1;
 } Fa2FwdParams;
 
 /* Host-only validation of `p` (no CUDA calls). Replaces the asserts and ValueErrors of

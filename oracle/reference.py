@@ -91,6 +91,29 @@ def naive_attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, causal=True, sm_
     return out
 
 
+def naive_attention_paged(q, k_cache, v_cache, block_table, cache_seqlens, causal=True, sm_scale=None,
+                          dtype=None, causal_align="bottom_right"):
+    """Paged K/V cache (an extension; the reference has no such mode): q [B, H_q, N_q, D] against
+    k/v caches [num_pages, page_size, H_kv, D], sequence b's key j in page block_table[b, j //
+    page_size], row j % page_size, cache_seqlens[b] keys. Each sequence's keys are gathered and
+    naive_attention runs on that sequence alone; a query that sees no key is zeros."""
+    dtype = dtype or q.dtype
+    B, H_q, N_q, D = q.shape
+    page_size = k_cache.shape[1]
+    out = torch.zeros(q.shape, dtype=dtype, device=q.device)
+    bt, sl = block_table.tolist(), [int(x) for x in cache_seqlens.tolist()]
+    for b in range(B):
+        n = sl[b]
+        if n == 0:
+            continue
+        pages = bt[b][:-(-n // page_size)]
+        ks = k_cache[pages].reshape(-1, *k_cache.shape[2:])[:n].transpose(0, 1).unsqueeze(0)  # [1, H_kv, n, D]
+        vs = v_cache[pages].reshape(-1, *v_cache.shape[2:])[:n].transpose(0, 1).unsqueeze(0)
+        o = naive_attention(q[b:b + 1], ks, vs, causal=causal, sm_scale=sm_scale, dtype=dtype, causal_align=causal_align)
+        out[b] = torch.nan_to_num(o, nan=0.0)[0]
+    return out
+
+
 def _tile_walk(n_kv, row_lo, row_hi, causal, block_n):
     """K/V column ranges a Q tile of rows [row_lo, row_hi) visits, with a mask flag:
     stage 1 = whole block_n tiles left of row_lo (no mask), stage 2 = the diagonal band up

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 def test_abi_version_and_struct_size():
     L = _lib.lib()
     assert L.fa2_sm100_abi_version() == _lib.ABI_VERSION
-    assert L.fa2_sm100_params_size() == ctypes.sizeof(_lib.Fa2FwdParams) == 272
+    assert L.fa2_sm100_params_size() == ctypes.sizeof(_lib.Fa2FwdParams) == 304
 
 
 def test_config_entry_point():

@@ -313,6 +313,11 @@ struct KArgs {
   // n_kv are the largest lengths. nullptr: fixed lengths n_q / n_kv, batch on the maps' b axis.
   const int* cu_q;
   const int* cu_kv;
+  // Paged K/V: sequence b's key j lives in page block_table[b * bt_stride + j / page_size], row
+  // j % page_size (the K/V tensor maps' b axis is the page, n the row); seqlens_kv[b] keys.
+  const int* block_table;
+  const int* seqlens_kv;
+  int bt_stride, page_size;
   void* o;                              // output base and element strides (h, n): used for the
   int64_t oh, on;                       // rows of a variable-length sequence's last O box
   int pack_shift;                       // pack == 1 << pack_shift (pack divides 128)
@@ -352,12 +357,12 @@ __host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, 
 
 // One work unit: packed Q rows [row0, row0 + 256) of batch b, q heads from hq0 (K/V head hkv),
 // against K/V tiles [j0, j0 + J) (in dual mode the second Q-tile slot walks [j0b, j0b + J)).
-// q0 / kv0: first Q / K/V position of the unit's sequence on the tensor maps' n axis, tb its
-// b coordinate (0 for a variable-length batch); n_q / n_kv / coff: the sequence's lengths and
-// causal shift.
+// q0 / kv0: first Q / K/V position of the unit's sequence on the tensor maps' n axis, tb / tbkv
+// the Q/O and K/V maps' b coordinate (0 for a packed token axis; paged K/V take their page per
+// tile); n_q / n_kv / coff: the sequence's lengths and causal shift.
 struct Unit {
   int x, b, hq0, hkv, row0, j0, j0b, J;
-  int q0, kv0, tb, n_q, n_kv, coff;
+  int q0, kv0, tb, tbkv, n_q, n_kv, coff;
 };
 
 // Unit slot n of this CTA; false when the CTA has no n-th slot. J == 0: the unit is empty (a
@@ -398,11 +403,26 @@ __device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
   u.j0 = 0;
   u.j0b = 0;
   if constexpr (VARLEN) {
-    u.q0 = __ldg(a.cu_q + u.b);
-    u.kv0 = __ldg(a.cu_kv + u.b);
-    u.n_q = __ldg(a.cu_q + u.b + 1) - u.q0;
-    u.n_kv = __ldg(a.cu_kv + u.b + 1) - u.kv0;
-    u.tb = 0;
+    // Per-sequence lengths: queries packed by cu_q or fixed; keys packed by cu_kv, counted by
+    // seqlens_kv (paged K/V) or fixed.
+    if (a.cu_q != nullptr) {
+      u.q0 = __ldg(a.cu_q + u.b);
+      u.n_q = __ldg(a.cu_q + u.b + 1) - u.q0;
+      u.tb = 0;
+    } else {
+      u.q0 = 0;
+      u.n_q = a.n_q;
+      u.tb = u.b;
+    }
+    if (a.cu_kv != nullptr) {
+      u.kv0 = __ldg(a.cu_kv + u.b);
+      u.n_kv = __ldg(a.cu_kv + u.b + 1) - u.kv0;
+      u.tbkv = 0;
+    } else {
+      u.kv0 = 0;
+      u.n_kv = a.seqlens_kv != nullptr ? __ldg(a.seqlens_kv + u.b) : a.n_kv;
+      u.tbkv = u.b;
+    }
     u.coff = a.bottom_right ? u.n_kv - u.n_q : 0;
     if (u.n_q < 0 || u.n_kv < 0 || u.n_q > a.n_q || u.n_kv > a.n_kv) {
       // Lengths the launch was not sized for: reported, and the unit is left out.
@@ -418,6 +438,7 @@ __device__ __forceinline__ bool get_unit(const KArgs& a, int n, Unit& u) {
     u.q0 = 0;
     u.kv0 = 0;
     u.tb = u.b;
+    u.tbkv = u.b;
     u.n_q = a.n_q;
     u.n_kv = a.n_kv;
     u.coff = a.causal_off;
@@ -680,10 +701,32 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           }
           mbar_arrive_expect_tx(bar(C::B_KV_FULL + st), C::TILE_BYTES);
           const CUtensorMap* m = is_v ? &tmV : &tmK;
+          const uint32_t dst = sbase + C::OFF_KV + st * C::TILE_BYTES;
+          if (VARLEN && a.block_table != nullptr) {
+            // Paged K/V: the tile's 128 keys are one page slice (page_size >= 128) or
+            // 128 / page_size whole pages, each a box of page_size rows at its row offset in the
+            // slot (a multiple of 8 rows, so the 128-byte swizzle lines up). Page slots past the
+            // sequence's last page are not read from the table: coordinate -1 loads zeros.
+            const int* bt = a.block_table + static_cast<int64_t>(u.b) * a.bt_stride;
+            const int pos = kv_tile * BN;
+            const int pages_used = (u.n_kv + a.page_size - 1) / a.page_size;
+            const int boxes = a.page_size >= BN ? 1 : BN / a.page_size;
+            for (int sub = 0; sub < boxes; ++sub) {
+              const int pi = pos / a.page_size + sub;
+              const int page = pi < pages_used ? __ldg(bt + pi) : -1;
+              const int row = a.page_size >= BN ? pos % a.page_size : 0;
 #pragma unroll
-          for (int c = 0; c < C::CHUNKS; ++c) {
-            tma_load_4d(sbase + C::OFF_KV + st * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
-                        bar(C::B_KV_FULL + st), c * 64, u.kv0 + kv_tile * BN, u.hkv, u.tb, pol_kv);
+              for (int c = 0; c < C::CHUNKS; ++c) {
+                tma_load_4d(dst + c * C::CHUNK_BYTES + sub * a.page_size * 128, m, bar(C::B_KV_FULL + st), c * 64,
+                            row, u.hkv, page, pol_kv);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < C::CHUNKS; ++c) {
+              tma_load_4d(dst + c * C::CHUNK_BYTES, m, bar(C::B_KV_FULL + st), c * 64, u.kv0 + kv_tile * BN, u.hkv,
+                          u.tbkv, pol_kv);
+            }
           }
           ++i;
           if (k == 0 && !dual) {
@@ -1212,7 +1255,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           // that reaches past its sequence's last position would overwrite the next sequence's
           // rows (the tensor map only clips at the end of the token axis), so such a box is
           // written row by row from registers instead.
-          const bool rowwise = VARLEN && pos0 + (32 >> min(a.pack_shift, 5)) > u.n_q;
+          const bool rowwise = VARLEN && a.cu_q != nullptr && pos0 + (32 >> min(a.pack_shift, 5)) > u.n_q;
           const int my_pos = (R0 + lane) >> a.pack_shift;
           uint16_t* my_row = static_cast<uint16_t*>(a.o) + static_cast<int64_t>(u.q0 + my_pos) * a.on +
                              static_cast<int64_t>(u.hq0 + ((R0 + lane) & (a.pack - 1))) * a.oh + epi_c0;
@@ -1284,7 +1327,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 // (gridDim.y is capped at 65535 by the host, xblocks may be larger).
 struct CombineArgs {
   int n_q, n_kv, pack, pack_shift, hblocks, rows_pad, num_splits, split_tiles, causal_off, xblocks;
-  int64_t ob, oh, on;  // output element strides (b, h, n); d stride is 1
+  int bottom_right;
+  const int* seqlens_kv;  // paged K/V: keys per sequence (n_kv and causal_off per batch); else nullptr
+  int64_t ob, oh, on;     // output element strides (b, h, n); d stride is 1
 };
 
 template <int D, bool CAUSAL, bool BF16>
@@ -1295,12 +1340,18 @@ fa2_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l
   const int R = blockIdx.x * 8 + warp;  // packed row within the (batch, head block) slice
   if (R >= c.n_q * c.pack) return;
   const int pos = R / c.pack;
-  const int J_cta = cta_kv_tiles<CAUSAL>(R / 256, c.n_q, c.n_kv, c.pack_shift, c.causal_off);
-  const int ns = min(c.num_splits, (J_cta + c.split_tiles - 1) / c.split_tiles);
   const int64_t xs = static_cast<int64_t>(c.xblocks);
   constexpr int PER = D / 32;  // columns per lane
   for (int x = static_cast<int>(blockIdx.y); x < c.xblocks; x += static_cast<int>(gridDim.y)) {
     const int b = x / c.hblocks;
+    int n_kv = c.n_kv, coff = c.causal_off;
+    if (c.seqlens_kv != nullptr) {
+      n_kv = __ldg(c.seqlens_kv + b);
+      coff = c.bottom_right ? n_kv - c.n_q : 0;
+    }
+    // The splits the forward kernel wrote for this row's 256-row block (at least one tile).
+    const int J_cta = max(1, cta_kv_tiles<CAUSAL>(R / 256, c.n_q, n_kv, c.pack_shift, coff));
+    const int ns = min(c.num_splits, (J_cta + c.split_tiles - 1) / c.split_tiles);
     const int h = (x % c.hblocks) * c.pack + R % c.pack;
     float mx = -INFINITY;
     for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, lse_part[(sp * xs + x) * c.rows_pad + R]);
@@ -1424,13 +1475,16 @@ SplitPlan plan_splits(const Fa2FwdParams* p) {
 template <int D, bool CAUSAL, bool BF16>
 int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   const bool split = plan_splits(p).num_splits > 1;
-  const bool is_varlen = p->cu_seqlens_q != nullptr;  // never together with split (validated)
-  auto kern = split ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, true, false>
-                    : (is_varlen ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false, true>
-                                 : fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false, false>);
+  // Per-sequence lengths (variable-length batch or paged K/V) take the VARLEN instantiation;
+  // split-KV comes with fixed lengths or paged K/V (not with cu_seqlens; validated).
+  const bool per_seq = p->cu_seqlens_q != nullptr || p->block_table != nullptr;
+  auto kern = split ? (per_seq ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, true, true>
+                               : fa2::fa2_fwd_kernel<D, CAUSAL, BF16, true, false>)
+                    : (per_seq ? fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false, true>
+                               : fa2::fa2_fwd_kernel<D, CAUSAL, BF16, false, false>);
   const int smem_alloc = split ? Cfg<D, true>::SMEM_ALLOC : Cfg<D, false>::SMEM_ALLOC;
-  const int variant = split ? 1 : (is_varlen ? 2 : 0);
-  static bool attr_done[3][kMaxDevices] = {};
+  const int variant = (split ? 1 : 0) + (per_seq ? 2 : 0);
+  static bool attr_done[4][kMaxDevices] = {};
   if (device < 0 || device >= kMaxDevices) return FA2_ERR_DEVICE;
   if (!attr_done[variant][device]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_alloc) != cudaSuccess) {
@@ -1454,10 +1508,14 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   const uint32_t gh_o = static_cast<uint32_t>(pack < 32 ? pack : 32);  // 32-row O box per warp
   const uint32_t obox[4] = {64, gh_o, 32u / gh_o, 1};
   // K / V: dims (d, n, h, b), 128-row boxes of one head.
-  const int64_t kdims[4] = {D, varlen ? p->total_kv : p->seqlen_kv, p->heads_kv, varlen ? 1 : p->batch};
+  // Paged K/V: dims (d, row in page, h, page); otherwise (d, n, h, b).
+  const bool paged = p->block_table != nullptr;
+  const int64_t kdims[4] = {D, paged ? p->page_size : (varlen ? p->total_kv : p->seqlen_kv), p->heads_kv,
+                            paged ? p->num_pages : (varlen ? 1 : p->batch)};
   const int64_t kstr[4] = {1, p->k_stride[2], p->k_stride[1], p->k_stride[0]};
   const int64_t vstr[4] = {1, p->v_stride[2], p->v_stride[1], p->v_stride[0]};
-  const uint32_t kvbox[4] = {64, static_cast<uint32_t>(fa2::BN), 1, 1};
+  const uint32_t kv_rows = static_cast<uint32_t>(paged && p->page_size < fa2::BN ? p->page_size : fa2::BN);
+  const uint32_t kvbox[4] = {64, kv_rows, 1, 1};
   const bool bf16 = (p->dtype == FA2_DTYPE_BF16);
   if (!make_map(&tmQ, bf16, p->q, qdims, qstr, qbox) || !make_map(&tmO, bf16, p->o, qdims, ostr, obox) ||
       !make_map(&tmK, bf16, p->k, kdims, kstr, kvbox) || !make_map(&tmV, bf16, p->v, kdims, vstr, kvbox)) {
@@ -1476,6 +1534,10 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.causal_off = (ka.bottom_right && !varlen) ? p->seqlen_kv - p->seqlen_q : 0;
   ka.cu_q = p->cu_seqlens_q;
   ka.cu_kv = p->cu_seqlens_kv;
+  ka.block_table = p->block_table;
+  ka.seqlens_kv = p->seqlens_kv;
+  ka.bt_stride = p->block_table_stride;
+  ka.page_size = p->page_size;
   ka.o = p->o;
   ka.oh = p->o_stride[1];
   ka.on = p->o_stride[2];
@@ -1528,6 +1590,8 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
     ca.num_splits = sp.num_splits;
     ca.split_tiles = sp.split_tiles;
     ca.causal_off = ka.causal_off;
+    ca.bottom_right = ka.bottom_right;
+    ca.seqlens_kv = paged ? p->seqlens_kv : nullptr;
     ca.xblocks = sp.xblocks;
     ca.ob = p->o_stride[0];
     ca.oh = p->o_stride[1];
@@ -1618,11 +1682,19 @@ int check_core(const Fa2FwdParams* p) {
   if (p->batch < 1 || p->heads_q < 1 || p->heads_kv < 1 || p->seqlen_q < 0 || p->seqlen_kv < 1) return FA2_ERR_SHAPE;
   if (p->causal_align != FA2_CAUSAL_TOP_LEFT && p->causal_align != FA2_CAUSAL_BOTTOM_RIGHT) return FA2_ERR_SHAPE;
   const bool varlen = p->cu_seqlens_q != nullptr || p->cu_seqlens_kv != nullptr;
+  const bool paged = p->block_table != nullptr || p->seqlens_kv != nullptr;
+  if (varlen && paged) return FA2_ERR_SHAPE;  // paged K/V come with fixed-length queries
   if (varlen) {
     // Per-sequence lengths live on the device; the causal mask applies per sequence, with its
     // alignment, whatever the lengths. Split-KV is not offered for variable-length batches.
     if (p->cu_seqlens_q == nullptr || p->cu_seqlens_kv == nullptr) return FA2_ERR_NULL;
     if (p->total_q < 0 || p->total_kv < 1 || p->num_splits > 1) return FA2_ERR_SHAPE;
+  } else if (paged) {
+    // Keys per sequence on the device (at most seqlen_kv); the causal mask applies per sequence.
+    if (p->block_table == nullptr || p->seqlens_kv == nullptr) return FA2_ERR_NULL;
+    const int ps = p->page_size;
+    if (!(ps == 16 || ps == 32 || ps == 64 || (ps >= 128 && ps % 128 == 0))) return FA2_ERR_SHAPE;
+    if (p->num_pages < 1 || p->block_table_stride < (p->seqlen_kv + ps - 1) / ps) return FA2_ERR_SHAPE;
   } else {
     if (p->causal && p->causal_align == FA2_CAUSAL_TOP_LEFT && p->seqlen_q != p->seqlen_kv) return FA2_ERR_SHAPE;
     if (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT && p->seqlen_q > p->seqlen_kv) return FA2_ERR_SHAPE;
@@ -1638,7 +1710,8 @@ int check_core(const Fa2FwdParams* p) {
   if ((rows + 255) / 256 > 65535) return FA2_ERR_SHAPE;
   if (static_cast<int64_t>(p->batch) * (p->heads_q / pack) > 0x7fffffffLL) return FA2_ERR_SHAPE;
   const int64_t qext[4] = {varlen ? 1 : p->batch, p->heads_q, varlen ? p->total_q : p->seqlen_q, p->head_dim};
-  const int64_t kext[4] = {varlen ? 1 : p->batch, p->heads_kv, varlen ? p->total_kv : p->seqlen_kv, p->head_dim};
+  const int64_t kext[4] = {paged ? p->num_pages : (varlen ? 1 : p->batch), p->heads_kv,
+                           paged ? p->page_size : (varlen ? p->total_kv : p->seqlen_kv), p->head_dim};
   if (!layout_ok(p->q_stride, qext) || !layout_ok(p->o_stride, qext) || !layout_ok(p->k_stride, kext) ||
       !layout_ok(p->v_stride, kext)) {
     return FA2_ERR_LAYOUT;

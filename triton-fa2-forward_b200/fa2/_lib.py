@@ -10,7 +10,7 @@ import os
 LIB_NAME = "libfa2_sm100.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 FA2_DTYPE_FP16 = 0
 FA2_DTYPE_BF16 = 1
@@ -81,6 +81,12 @@ class Fa2FwdParams(ctypes.Structure):
         ("cu_seqlens_kv", ctypes.c_void_p),
         ("total_q", ctypes.c_int32),
         ("total_kv", ctypes.c_int32),
+        ("block_table", ctypes.c_void_p),
+        ("seqlens_kv", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("reserved1", ctypes.c_int32),
     ]
 
 
@@ -151,7 +157,8 @@ def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stri
                 batch, heads_q, heads_kv, seqlen_q, seqlen_kv, head_dim, dtype, causal,
                 pack_gqa, qk_scale, err_flag=0, timeout_cycles=0, gate=0, num_splits=1,
                 workspace=0, workspace_bytes=0, causal_align=FA2_CAUSAL_TOP_LEFT,
-                cu_seqlens_q=0, cu_seqlens_kv=0, total_q=0, total_kv=0):
+                cu_seqlens_q=0, cu_seqlens_kv=0, total_q=0, total_kv=0, block_table=0, seqlens_kv=0,
+                block_table_stride=0, page_size=0, num_pages=0):
     p = Fa2FwdParams()
     p.q, p.k, p.v, p.o = q_ptr, k_ptr, v_ptr, o_ptr
     p.q_stride[:] = list(q_stride)
@@ -172,6 +179,9 @@ def make_params(q_ptr, k_ptr, v_ptr, o_ptr, q_stride, k_stride, v_stride, o_stri
     p.cu_seqlens_q = cu_seqlens_q or None
     p.cu_seqlens_kv = cu_seqlens_kv or None
     p.total_q, p.total_kv = int(total_q), int(total_kv)
+    p.block_table = block_table or None
+    p.seqlens_kv = seqlens_kv or None
+    p.block_table_stride, p.page_size, p.num_pages = int(block_table_stride), int(page_size), int(num_pages)
     return p
 
 

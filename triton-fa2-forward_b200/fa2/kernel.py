@@ -22,9 +22,12 @@ Differences from the reference that do not change results:
   * head_dim 16 and 32 run the 64 kernel on zero-padded copies (extra zero columns add
     nothing to QK^T and produce zero output columns that are dropped).
 
-Also (no counterpart in the reference, whose README lists variable-length batches out of scope):
+Also (no counterpart in the reference, whose README lists variable-length batches and paged K/V
+out of scope):
     attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal=True, ...)
-with q [total_q, H_q, D], k/v [total_k, H_kv, D] packed along one token axis.
+with q [total_q, H_q, D], k/v [total_k, H_kv, D] packed along one token axis, and
+    attention_kvcache(q, k_cache, v_cache, block_table, cache_seqlens, causal=True, ...)
+with q [B, H_q, N_q, D] against a paged K/V cache [num_pages, page_size, H_kv, D].
 
 Extensions (keyword arguments the reference does not have; their defaults keep its behaviour):
   * causal_align="bottom_right": the causal mask lines the last query up with the last key
@@ -318,6 +321,92 @@ def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seql
             rc = launch(q, k, v, out, pack)
         if rc in (_lib.FA2_ERR_LAYOUT, _lib.FA2_ERR_TMA_ENCODE):
             qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+            oc = torch.empty_like(qc)
+            rc = launch(qc, kc, vc, oc, pack)
+            if rc == _lib.FA2_OK:
+                out.copy_(oc)
+        if rc != _lib.FA2_OK:
+            raise _lib.Fa2Error(rc, _lib.strerror(rc))
+        if _sync_check_enabled():
+            check_device_errors(q.device)
+    return out
+
+
+def attention_kvcache(q, k_cache, v_cache, block_table, cache_seqlens, max_seqlen_k=None, causal=True,
+                      sm_scale=None, pack_gqa=None, causal_align="bottom_right", num_splits=None):
+    """Attention of new queries against a paged K/V cache (the layout of flash_attn_with_kvcache).
+    An extension: the reference has no such entry point.
+
+    q: [B, H_q, N_q, D]; k_cache, v_cache: [num_pages, page_size, H_kv, D] (page_size 16, 32, 64 or a
+    multiple of 128); block_table: int32 CUDA [B, pages_per_seq], sequence b's key j living in page
+    block_table[b, j // page_size], row j % page_size; cache_seqlens: int32 CUDA [B], keys per
+    sequence. max_seqlen_k bounds them (default: pages_per_seq * page_size; a longer sequence is
+    reported as a device error). The causal mask is per sequence, bottom-right by default (the new
+    queries are the sequence's last N_q positions). Split-KV as in attention(). Returns
+    [B, H_q, N_q, D], asynchronously.
+    """
+    assert q.dim() == 4 and k_cache.dim() == 4 and v_cache.shape == k_cache.shape
+    B, H_q, N_q, D = q.shape
+    num_pages, page_size, H_kv, Dk = k_cache.shape
+    assert Dk == D and D in (64, 128), "paged K/V needs head_dim 64 or 128"
+    assert q.dtype == k_cache.dtype == v_cache.dtype and q.dtype in (torch.float16, torch.bfloat16)
+    assert H_q % H_kv == 0, "GQA needs H_q divisible by H_kv"
+    assert causal_align in CAUSAL_ALIGNS, f"causal_align must be one of {sorted(CAUSAL_ALIGNS)}"
+    assert page_size in (16, 32, 64) or (page_size >= 128 and page_size % 128 == 0), "page_size"
+    assert block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.shape[0] == B
+    assert cache_seqlens.dtype == torch.int32 and cache_seqlens.shape == (B,)
+    if not (q.is_cuda and k_cache.is_cuda and v_cache.is_cuda and block_table.is_cuda and cache_seqlens.is_cuda):
+        raise RuntimeError("fa2.kernel.attention_kvcache runs only on an sm_100 CUDA device (no CPU path)")
+    if max_seqlen_k is None:
+        max_seqlen_k = block_table.shape[1] * page_size
+    group = H_q // H_kv
+    if pack_gqa is None:
+        pack_gqa = group > 1 and KERNEL_BLOCK_M % group == 0
+    elif pack_gqa and KERNEL_BLOCK_M % group:
+        raise ValueError(f"pack_gqa needs BLOCK_M ({KERNEL_BLOCK_M}) to be a multiple of the GQA group ({group})")
+    pack = bool(pack_gqa) and group > 1
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if not sm_scale > 0:
+        raise ValueError(f"sm_scale must be positive (the row max is scaled after it is taken), got {sm_scale}")
+    out = torch.empty_like(q)
+    if out.numel() == 0:
+        return out
+    if max_seqlen_k == 0:
+        return out.zero_()
+    if num_splits is None:
+        num_splits = auto_num_splits(B, H_q, N_q, max_seqlen_k, group, group if pack else 1, causal,
+                                     causal_align=causal_align)
+    num_splits = max(1, int(num_splits))
+    bt, sl = block_table.contiguous(), cache_seqlens.contiguous()
+    kst = lambda t: (int(t.stride(0)), int(t.stride(2)), int(t.stride(1)), int(t.stride(3)))  # noqa: E731
+
+    def launch(qq, kk, vv, oo, pk):
+        err = _err_word(qq.device)
+        p = _lib.make_params(
+            qq.data_ptr(), kk.data_ptr(), vv.data_ptr(), oo.data_ptr(), _strides(qq), kst(kk), kst(vv), _strides(oo),
+            B, H_q, H_kv, N_q, int(max_seqlen_k), D,
+            _lib.FA2_DTYPE_BF16 if qq.dtype == torch.bfloat16 else _lib.FA2_DTYPE_FP16,
+            causal, pk, sm_scale * LOG2E, err.data_ptr(), 0, num_splits=num_splits,
+            causal_align=CAUSAL_ALIGNS[causal_align], block_table=bt.data_ptr(), seqlens_kv=sl.data_ptr(),
+            block_table_stride=bt.shape[1], page_size=page_size, num_pages=num_pages)
+        ws = None
+        if num_splits > 1:
+            nbytes = _lib.workspace_bytes(p)
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=qq.device)
+            p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
+        rc = _lib.launch(p, torch.cuda.current_stream(qq.device).cuda_stream)
+        if ws is not None:
+            ws.record_stream(torch.cuda.current_stream(qq.device))
+        return rc
+
+    with torch.cuda.device(q.device):
+        rc = launch(q, k_cache, v_cache, out, pack)
+        if rc == _lib.FA2_ERR_TMA_ENCODE and pack:
+            pack = False
+            rc = launch(q, k_cache, v_cache, out, pack)
+        if rc in (_lib.FA2_ERR_LAYOUT, _lib.FA2_ERR_TMA_ENCODE):
+            qc, kc, vc = q.contiguous(), k_cache.contiguous(), v_cache.contiguous()
             oc = torch.empty_like(qc)
             rc = launch(qc, kc, vc, oc, pack)
             if rc == _lib.FA2_OK:
