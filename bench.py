@@ -248,6 +248,48 @@ def decode_secondary(dev, steps=10):
             "launches_per_step": 2}
 
 
+def decode_paged_secondary(dev, steps=10, page_size=256):
+    """Secondary workload: the decode shape of decode_secondary with K/V in a paged cache (pages of
+    page_size keys handed out in a shuffled order, fa2.kernel.attention_kvcache). Algorithmic bytes
+    as decode_secondary; reported against the measured copy peak."""
+    from fa2.kernel import attention_kvcache
+
+    B, Hq, Hkv, Nkv, D = 4, 32, 8, 65536, 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    pages = B * Nkv // page_size
+    q = torch.randn(B, Hq, 1, D, device=dev, dtype=torch.bfloat16, generator=g)
+    k = torch.randn(pages, page_size, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+    v = torch.randn(pages, page_size, Hkv, D, device=dev, dtype=torch.bfloat16, generator=g)
+    bt = torch.randperm(pages, device=dev, generator=g).to(torch.int32).reshape(B, Nkv // page_size)
+    sl = torch.full((B,), Nkv, dtype=torch.int32, device=dev)
+    fn = lambda: attention_kvcache(q, k, v, bt, sl, causal=True)  # noqa: E731
+    for _ in range(3):
+        fn()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ts = []
+    for _ in range(steps):
+        flush.fill_(1)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize(dev)
+        ts.append(s.elapsed_time(e))
+    ms = sum(ts) / len(ts)
+    nbytes = 2 * k.numel() * 2 + 2 * q.numel() * 2
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["hbm_gbs"])
+    except Exception:
+        peak = 6650.0
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": f"decode, paged K/V: B={B} Hq={Hq} Hkv={Hkv} N_q=1 N_kv={Nkv} D={D} bf16, "
+                        f"pages of {page_size} keys in shuffled order, bottom-right causal",
+            "ms": ms, "GB/s": gbs, "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak,
+                                                "unit": "GB/s", "frac": gbs / peak},
+            "launches_per_step": 2}
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference's CPU path timed on the host cores (rank 0 only)."""
     if rank != 0:
@@ -443,9 +485,10 @@ def run_ours(args, world, rank, local):
     triton_ref = None
     if rank == 0 and world == 1 and not args.no_triton_ref:
         triton_ref = triton_reference_same_box(q, k, v)
-    decode = None
+    decode = decode_paged = None
     if rank == 0 and world == 1 and not args.no_secondary:
         decode = decode_secondary(dev)
+        decode_paged = decode_paged_secondary(dev)
 
     if pg is not None:
         pg.barrier()
@@ -485,6 +528,8 @@ def run_ours(args, world, rank, local):
         line["reference_triton_same_gpu"] = triton_ref
     if decode is not None:
         line["secondary_decode"] = decode
+    if decode_paged is not None:
+        line["secondary_decode_paged"] = decode_paged
     print(json.dumps(line), flush=True)
     return 0
 
