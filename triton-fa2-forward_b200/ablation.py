@@ -12,7 +12,9 @@ Every variant computes the full attention (no work is skipped); they differ only
   emu_50         half of the exp2 on the FMA pipe at both head dims
   emu_25_pairs_0/1/2   25% at D=128 on pairs 0,4,8,12 / 1,5,9,13 / 2,6,10,14 of each chunk
                  (shipped: 3, 7, 11, 15)
-  emu_d64_12     12.5% (pairs 7, 15) on the FMA pipe at D=64 for fp16 too (shipped: bf16 only)
+  d64_fp16_all_mufu   every exp2 on the MUFU at D=64 fp16 (shipped: pairs 7, 15 on the FMA pipe)
+  d64_emu_pairs_3_11, d64_emu_3pairs   at D=64, pairs 3, 11 (12.5%) or 5, 10, 15 (18.75%) on the
+                 FMA pipe instead of 7, 15
   d64_bf16_all_mufu   every exp2 on the MUFU at D=64 bf16
   emu_12, emu_12_pairs_7, emu_37   12.5% (pairs 1,9 / 7,15) or 37.5% on the FMA pipe at D=128
   p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
@@ -31,13 +33,14 @@ Every variant computes the full attention (no work is skipped); they differ only
                  (shipped: four of 32 columns at D=128, one of 128 at D=64)
   d128_s_load_x128, d64_s_load_x32   the other load width at one head dim
   d64_regs_208   208 / 88 registers at D=64 only
-  fp16_poly_deg3 the degree-3 exp2 polynomial for fp16 P too (shipped: degree 4), with pairs 7 and
-                 15 on the FMA pipe at D=64 fp16 (shipped: none)
+  fp16_poly_deg3 the degree-3 exp2 polynomial for fp16 P too (shipped: degree 4)
   row_split_2    two softmax warps per row quadrant, 64 scores each, exchanging the row max and
                  row sum through TMEM (FA2_ROW_SPLIT=2: 20 warps, setmaxnreg 104/64) instead of
                  one warp taking all 128 scores (12 warps, 200/104)
   row_major_noncausal   without a causal mask, the persistent CTAs walk the units row block by
                  row block (FA2_HEAD_MAJOR=0) instead of (batch, head) slice by slice
+  d64_sep_p      at D=64, P in TMEM columns of its own and the next QK of a tile issued as soon as
+                 its scores are read (FA2_SEP_P_D64=1) instead of P overwriting S_t
   seq_exp        the two softmax warps of a lane quadrant take turns on the exponential phase of
                  a step (FA2_SEQ_EXP=1, a bounded mbarrier hand-shake) instead of running freely
   ffma_pass      s * qk_scale - m for the whole row in one FMA pass before the exponentials
@@ -79,7 +82,9 @@ COMPILED = {
     "emu_25_pairs_2": ["-DFA2_EMU_MASK_D128=0x4444u"],
     "emu_12": ["-DFA2_EMU_MASK_D128=0x0202u"],
     "emu_12_pairs_7": ["-DFA2_EMU_MASK_D128=0x8080u"],
-    "emu_d64_12": ["-DFA2_EMU_MASK_D64=0x8080u"],
+    "d64_fp16_all_mufu": ["-DFA2_EMU_MASK_D64=0x0u"],
+    "d64_emu_pairs_3_11": ["-DFA2_EMU_MASK_D64=0x0808u", "-DFA2_EMU_MASK_D64_BF16=0x0808u"],
+    "d64_emu_3pairs": ["-DFA2_EMU_MASK_D64=0x8420u", "-DFA2_EMU_MASK_D64_BF16=0x8420u"],
     "d64_bf16_all_mufu": ["-DFA2_EMU_MASK_D64_BF16=0x0u"],
     "emu_37": ["-DFA2_EMU_MASK_D128=0x2A2Au"],
     "p_split_2": ["-DFA2_P_SPLIT=2"],
@@ -98,8 +103,9 @@ COMPILED = {
     "d128_s_load_x128": ["-DFA2_S_LOAD_X_D128=128"],
     "d64_s_load_x32": ["-DFA2_S_LOAD_X_D64=32"],
     "d64_regs_208": ["-DFA2_REGS_SOFTMAX_D64=208"],
-    "fp16_poly_deg3": ["-DFA2_POLY_DEG_FP16=3", "-DFA2_EMU_MASK_D64=0x8080u"],
+    "fp16_poly_deg3": ["-DFA2_POLY_DEG_FP16=3"],
     "seq_exp": ["-DFA2_SEQ_EXP=1"],
+    "d64_sep_p": ["-DFA2_SEP_P_D64=1"],
     "row_major_noncausal": ["-DFA2_HEAD_MAJOR=0"],
     "ffma_pass": ["-DFA2_FFMA_PASS=1"],
     "seq_exp_ffma_pass": ["-DFA2_SEQ_EXP=1", "-DFA2_FFMA_PASS=1"],

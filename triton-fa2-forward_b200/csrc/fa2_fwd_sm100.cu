@@ -120,8 +120,8 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // Which of the 16 exp2 pairs of a 32-column chunk run on the FMA pipe (the rest on the MUFU).
 // D = 128: pairs 3, 7, 11, 15, i.e. 25% on the FMA pipe (the same share on pairs 1, 5, 9, 13
 // measured 1.4% slower on two boxes; 37.5% is 6% slower). D = 64 has half the tensor work per
-// score and less pipe headroom for the polynomial: bf16 (degree-3 polynomial) puts pairs 7 and
-// 15 on the FMA pipe (12.5%, +2..5% over all-MUFU), fp16 (degree 4) runs every exp2 on the MUFU.
+// score and less pipe headroom for the polynomial: pairs 7 and 15 (12.5%) on the FMA pipe, for
+// bf16 (degree-3 polynomial, +7% over all-MUFU) and fp16 (degree 4, +5%); 25% is slower for both.
 #ifndef FA2_POLY_DEG_FP16
 #define FA2_POLY_DEG_FP16 4  // degree of the FMA-pipe exp2 polynomial when P is rounded to fp16
 #endif
@@ -129,7 +129,7 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #define FA2_EMU_MASK_D128 0x8888u
 #endif
 #ifndef FA2_EMU_MASK_D64
-#define FA2_EMU_MASK_D64 0x0u
+#define FA2_EMU_MASK_D64 0x8080u
 #endif
 #ifndef FA2_EMU_MASK_D64_BF16
 #define FA2_EMU_MASK_D64_BF16 0x8080u
@@ -179,6 +179,15 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #endif
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
+#endif
+#ifndef FA2_SEP_P_D64
+// 1: at D = 64 (outside split-KV) P_t gets its own 64 TMEM columns (S 0-255, O 256-383, P 384-511)
+// instead of overwriting the upper half of S_t, so the next QK of a tile is issued as soon as its
+// softmax warps have loaded S_t, not after the PV that reads P. Measured 9-12% slower (D = 64 fp16
+// and bf16, causal and not): before rewriting P_t a softmax warp must now wait for the previous
+// PV, which queues behind the other tile's GEMMs, where S_t(j + 1) arriving used to imply it.
+// 0 (shipped): P overwrites S_t, as at D = 128 (which has no TMEM left for a separate P).
+#define FA2_SEP_P_D64 0
 #endif
 #ifndef FA2_HEAD_MAJOR
 // 1: without a causal mask the persistent CTAs walk the units (batch, head) slice by slice;
@@ -260,12 +269,17 @@ struct Cfg {
   static constexpr int B_Q_EMPTY = 11 + 2 * STAGES; // [2]  last QK of tile t of a unit retired: Q_t reloadable
   static constexpr int B_XCH = 13 + 2 * STAGES;     // [8]  (HALVES == 2) row-pair exchange of tile t, quadrant q
   static constexpr int B_SEQ = 13 + 2 * STAGES;     // [8]  (FA2_SEQ_EXP) exponential phase of tile t, quadrant q done
-  static constexpr int NUM_BARS = 13 + 2 * STAGES + ((HALVES == 2 || FA2_SEQ_EXP) ? 8 : 0);
+  static constexpr int B_S_EMPTY = 21 + 2 * STAGES; // [2]  (SEP_P) S_t read by the softmax warps: the next QK may write it
+  static constexpr int B_P_EMPTY = 23 + 2 * STAGES; // [2]  (SEP_P) PV(t) retired: P_t may be rewritten, O_t rescaled
+  static constexpr int NUM_BARS = 25 + 2 * STAGES;
+  // P_t in TMEM columns of its own (see FA2_SEP_P_D64), for the fixed-length D = 64 build.
+  static constexpr bool SEP_P = D == 64 && !SPLIT && HALVES == 1 && !FA2_TWO_ISSUERS && FA2_SEP_P_D64 != 0;
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
   static constexpr int TMEM_O = 2 * BN;                 // O_t at TMEM_O + t * D
-  static_assert(TMEM_O + 2 * D <= TMEM_COLS, "TMEM budget");
+  static constexpr int TMEM_P = TMEM_O + 2 * D;         // SEP_P: P_t at TMEM_P + t * BN / 2
+  static_assert(TMEM_O + 2 * D + (SEP_P ? BN : 0) <= TMEM_COLS, "TMEM budget");
   // HALVES == 2: column that carries warp h's row sum to the other warp of the row in the
   // epilogue. D = 128: the first of its own O columns (read before it is overwritten);
   // D = 64: spare columns past O_1.
@@ -571,6 +585,12 @@ __device__ __forceinline__ void rescale_o_cols(uint32_t tO, float alpha) {
   tmem_wait_st();
 }
 
+// Every lane waits for `bar`'s phase; true when it completed for the whole warp.
+__device__ __forceinline__ bool warp_wait_pv(uint32_t bar, uint32_t parity, const KArgs& a) {
+  const bool w = mbar_wait(bar, parity, a.timeout, a.err);
+  return __all_sync(0xffffffffu, w);
+}
+
 // ------------------------------------------------------------------------ kernel
 // SPLIT: the split-KV build (num_splits > 1); VARLEN: the variable-length build
 // (cu_seqlens given). The host launches each exactly then; never both.
@@ -612,6 +632,10 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     }
     if constexpr (FA2_SEQ_EXP != 0) {
       for (int x = 0; x < 8; ++x) mbar_init(bar(C::B_SEQ + x), 32);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(bar(C::B_S_EMPTY + t), BM);  // every softmax thread of the tile
+      mbar_init(bar(C::B_P_EMPTY + t), 1);   // the MMA thread's commit
     }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(C::B_KV_FULL + s), 1);
@@ -780,8 +804,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 #pragma unroll
           for (int kk = kk0; kk < kk1; ++kk) {
             const int k0 = h * SCOLS + kk * 16;  // first score (V row) of this k-step
-            mma_ts(tmem + C::TMEM_O + t * D, tmem + t * BN + h * SCOLS + P_OFF + kk * 8,
-                   vd + static_cast<uint64_t>((k0 * 128) >> 4), idesc_pv, (acc || k0 > 0) ? 1u : 0u);
+            const uint32_t p_col = C::SEP_P ? C::TMEM_P + t * (BN / 2) + kk * 8 : t * BN + h * SCOLS + P_OFF + kk * 8;
+            mma_ts(tmem + C::TMEM_O + t * D, tmem + p_col, vd + static_cast<uint64_t>((k0 * 128) >> 4), idesc_pv,
+                   (acc || k0 > 0) ? 1u : 0u);
           }
         }
       };
@@ -846,6 +871,70 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
               }
             }
             if (!ok) break;
+          }
+        } while (false);
+      } else if (C::SEP_P && issuers == 1) {
+        // P in its own TMEM columns: in step j the next QK of each tile (step j + 1, or the next
+        // unit's step 0) goes first, as soon as that tile's softmax warps have read S_t(j)
+        // (S_EMPTY); then PV(0, j) and PV(1, j) as P arrives. Each PV is followed by a commit on
+        // P_EMPTY(t), which lets the softmax warps rewrite P_t and rescale O_t. Ring order stays
+        // the loader's (K_j, V_j, K_j+1, ...): K_j+1 is consumed before V_j.
+        do {
+          if (!mwait(C::B_Q + 0, 0) || !kv_wait(0)) { ok = false; break; }
+          tc_fence_after();
+          issue_qk(0, 0);
+          mma_commit(bar(C::B_S_FULL + 0));
+          if (u.J == 1) mma_commit(bar(C::B_Q_EMPTY + 0));
+          if (!mwait(C::B_Q + 1, 0)) { ok = false; break; }
+          tc_fence_after();
+          issue_qk(1, 0);
+          mma_commit(bar(C::B_S_FULL + 1));
+          mma_commit(bar(C::B_KV_EMPTY + 0));
+          if (u.J == 1) mma_commit(bar(C::B_Q_EMPTY + 1));
+          int n = 0, i = 0, g = 0;  // unit, ring position of its K_0, steps of the units before
+          while (true) {
+            Unit nx;
+            int slot_next = slot;
+            const bool has_next = next_unit<CAUSAL, VARLEN>(a, slot_next, nx);
+            const uint32_t qph_next = static_cast<uint32_t>(n + 1) & 1u;
+            for (int j = 0; j < u.J; ++j) {
+              const bool last = (j + 1 == u.J);
+              const int iv = i + 2 * j + 1, ik = i + 2 * j + 2;
+              const int sv = iv % C::STAGES, sk = ik % C::STAGES;
+              const bool more = !last || has_next;
+              // The QK issued here is its unit's last one for tile t: Q_t may be reloaded after it.
+              const bool qk_final = last ? (has_next && nx.J == 1) : (j + 2 == u.J);
+              const uint32_t pph = static_cast<uint32_t>(g + j) & 1u;
+              if (more) {
+                if (!kv_wait(ik)) { ok = false; break; }
+                for (int t = 0; t < 2; ++t) {
+                  if (!mwait(C::B_S_EMPTY + t, pph) || (last && !mwait(C::B_Q + t, qph_next))) {
+                    ok = false;
+                    break;
+                  }
+                  tc_fence_after();
+                  issue_qk(t, sk);
+                  mma_commit(bar(C::B_S_FULL + t));
+                  if (qk_final) mma_commit(bar(C::B_Q_EMPTY + t));
+                }
+                if (!ok) break;
+                mma_commit(bar(C::B_KV_EMPTY + sk));
+              }
+              if (!kv_wait(iv)) { ok = false; break; }
+              for (int t = 0; t < 2; ++t) {
+                if (!pv_tile(t, sv, j > 0, pph)) { ok = false; break; }
+                mma_commit(bar(C::B_P_EMPTY + t));
+                if (last) mma_commit(bar(C::B_O_FULL + t));
+              }
+              if (!ok) break;
+              mma_commit(bar(C::B_KV_EMPTY + sv));
+            }
+            if (!ok || !has_next) break;
+            i += 2 * u.J;
+            g += u.J;
+            ++n;
+            u = nx;
+            slot = slot_next;
           }
         } while (false);
       } else if (issuers == 2) {
@@ -968,7 +1057,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t tS = tmem + lane_addr + t * BN + h * SCOLS;            // this warp's scores
     [[maybe_unused]] const uint32_t tS_other = tmem + lane_addr + t * BN + (h ^ 1) * SCOLS;  // the other warp's (HALVES == 2)
-    const uint32_t tP = tS + P_OFF;
+    const uint32_t tP = C::SEP_P ? tmem + lane_addr + C::TMEM_P + t * (BN / 2) : tS + P_OFF;
     const uint32_t tO = tmem + lane_addr + C::TMEM_O + t * D;
     const float qk_scale = a.qk_scale;
     const uint64_t sc2 = f2_pack(qk_scale, qk_scale);
@@ -1053,6 +1142,22 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < NCH; ++c) reg_fence32(s[c]);
+        if constexpr (C::SEP_P) {
+          // S_t is in registers: the MMA warp may compute the next S_t over it.
+          tc_fence_before();
+          mbar_arrive(bar(C::B_S_EMPTY + t));
+        }
+        // SEP_P: P_t and O_t are still in use by PV(t) of the step before (issued after the next
+        // QK); wait for it before the first P store or O rescale of this step.
+        auto p_empty_wait = [&]() -> bool {
+          if constexpr (C::SEP_P) {
+            if (g + j > 0) {
+              if (!warp_wait_pv(bar(C::B_P_EMPTY + t), static_cast<uint32_t>(g + j - 1) & 1u, a)) return false;
+              tc_fence_after();
+            }
+          }
+          return true;
+        };
         if (spec_max<D>() && !masked && j > 0 && __all_sync(0xffffffffu, m_use != -INFINITY)) {
           // P with the current reference max while the row max is taken (the two are independent
           // and use different pipes); the threshold test then runs before the hand-off.
@@ -1063,7 +1168,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           // Pass 0 uses the current reference max. If some row's max moved past the threshold
           // (rare), pass 1 moves it, rescales this warp's O_t columns (PV(t, j-1) has retired:
           // S_t(j) was committed after it) and redoes these chunks with the new reference max.
-          if (!seq_wait(j)) { ok = false; break; }
+          if (!seq_wait(j) || !p_empty_wait()) { ok = false; break; }
 #pragma unroll 1
           for (int pass = 0;; ++pass) {
 #pragma unroll
@@ -1125,6 +1230,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           alpha = ex2_mufu(m_use - m_cand);
           m_use = m_cand;
         }
+        if (!p_empty_wait()) { ok = false; break; }
         if (j > 0 && __any_sync(0xffffffffu, bump)) {
           // PV(t, j-1) has retired: S_t(j) was committed after it.
           rescale_o_cols<RCOLS>(tO + h * RCOLS, alpha);

@@ -28,6 +28,7 @@ CONFIGS = {
     # the other dtype at each head dim (design-choice ablation)
     "mha_causal_fp16": (4, 16, 16, 4096, 128, torch.float16, True, 1.0),
     "full_long_bf16": (2, 32, 32, 16384, 64, torch.bfloat16, False, 0.5),
+    "mha_causal_d64": (4, 16, 16, 4096, 64, torch.bfloat16, True, 1.0),
     "mqa_causal": (2, 32, 1, 4096, 128, torch.bfloat16, True, 1.0),
 }
 
