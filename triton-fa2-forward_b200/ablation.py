@@ -33,12 +33,14 @@ Every variant computes the full attention (no work is skipped); they differ only
                  (shipped: four of 32 columns at D=128, one of 128 at D=64)
   d128_s_load_x128, d64_s_load_x32   the other load width at one head dim
   d64_regs_208   208 / 88 registers at D=64 only
-  fp16_poly_deg3 the degree-3 exp2 polynomial for fp16 P too (shipped: degree 4)
+  fp16_poly_deg4 the degree-4 exp2 polynomial for fp16 P (shipped: degree 3, as for bf16)
   row_split_2    two softmax warps per row quadrant, 64 scores each, exchanging the row max and
                  row sum through TMEM (FA2_ROW_SPLIT=2: 20 warps, setmaxnreg 104/64) instead of
                  one warp taking all 128 scores (12 warps, 200/104)
   row_major_noncausal   without a causal mask, the persistent CTAs walk the units row block by
                  row block (FA2_HEAD_MAJOR=0) instead of (batch, head) slice by slice
+  defer_epi      a unit's output written during the next unit's first step, after its P hand-off
+                 (FA2_DEFER_EPI=1) instead of when the unit ends
   d64_sep_p      at D=64, P in TMEM columns of its own and the next QK of a tile issued as soon as
                  its scores are read (FA2_SEP_P_D64=1) instead of P overwriting S_t
   seq_exp        the two softmax warps of a lane quadrant take turns on the exponential phase of
@@ -103,9 +105,10 @@ COMPILED = {
     "d128_s_load_x128": ["-DFA2_S_LOAD_X_D128=128"],
     "d64_s_load_x32": ["-DFA2_S_LOAD_X_D64=32"],
     "d64_regs_208": ["-DFA2_REGS_SOFTMAX_D64=208"],
-    "fp16_poly_deg3": ["-DFA2_POLY_DEG_FP16=3"],
+    "fp16_poly_deg4": ["-DFA2_POLY_DEG_FP16=4"],
     "seq_exp": ["-DFA2_SEQ_EXP=1"],
     "d64_sep_p": ["-DFA2_SEP_P_D64=1"],
+    "defer_epi": ["-DFA2_DEFER_EPI=1"],
     "row_major_noncausal": ["-DFA2_HEAD_MAJOR=0"],
     "ffma_pass": ["-DFA2_FFMA_PASS=1"],
     "seq_exp_ffma_pass": ["-DFA2_SEQ_EXP=1", "-DFA2_FFMA_PASS=1"],

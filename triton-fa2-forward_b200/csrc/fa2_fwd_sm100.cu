@@ -123,7 +123,9 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // score and less pipe headroom for the polynomial: pairs 7 and 15 (12.5%) on the FMA pipe, for
 // bf16 (degree-3 polynomial, +7% over all-MUFU) and fp16 (degree 4, +5%); 25% is slower for both.
 #ifndef FA2_POLY_DEG_FP16
-#define FA2_POLY_DEG_FP16 4  // degree of the FMA-pipe exp2 polynomial when P is rounded to fp16
+// Degree of the FMA-pipe exp2 polynomial when P is rounded to fp16. Degree 3 (max rel. error
+// 7.5e-5, below half an fp16 ulp, 2^-11 = 4.9e-4) measured +2.6% at D = 64 over degree 4 (2.7e-6).
+#define FA2_POLY_DEG_FP16 3
 #endif
 #ifndef FA2_EMU_MASK_D128
 #define FA2_EMU_MASK_D128 0x8888u
@@ -179,6 +181,15 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #endif
 #ifndef FA2_PERSISTENT
 #define FA2_PERSISTENT 1  // 0: one CTA per work unit (the grid covers the units) without split-KV too
+#endif
+#ifndef FA2_DEFER_EPI
+// 1: a softmax warp writes a unit's output during the next unit's first step, after that step's
+// P hand-off (where it would otherwise wait for the next S), instead of between the units; the
+// next unit's first PV, which overwrites O_t, waits on O_EMPTY until O_t is in registers.
+// Measured 1-3.4% slower (headline, MHA causal, pack_tail; same box, with or without the branch
+// marked cold), like moving the epilogue to warps of its own. 0 (shipped): the epilogue runs
+// when the unit ends.
+#define FA2_DEFER_EPI 0
 #endif
 #ifndef FA2_SEP_P_D64
 // 1: at D = 64 (outside split-KV) P_t gets its own 64 TMEM columns (S 0-255, O 256-383, P 384-511)
@@ -271,9 +282,12 @@ struct Cfg {
   static constexpr int B_SEQ = 13 + 2 * STAGES;     // [8]  (FA2_SEQ_EXP) exponential phase of tile t, quadrant q done
   static constexpr int B_S_EMPTY = 21 + 2 * STAGES; // [2]  (SEP_P) S_t read by the softmax warps: the next QK may write it
   static constexpr int B_P_EMPTY = 23 + 2 * STAGES; // [2]  (SEP_P) PV(t) retired: P_t may be rewritten, O_t rescaled
-  static constexpr int NUM_BARS = 25 + 2 * STAGES;
+  static constexpr int B_O_EMPTY = 25 + 2 * STAGES; // [2]  (DEFER) O_t of the previous unit in registers: PV may overwrite it
+  static constexpr int NUM_BARS = 27 + 2 * STAGES;
   // P_t in TMEM columns of its own (see FA2_SEP_P_D64), for the fixed-length D = 64 build.
   static constexpr bool SEP_P = D == 64 && !SPLIT && HALVES == 1 && !FA2_TWO_ISSUERS && FA2_SEP_P_D64 != 0;
+  // Deferred epilogue (FA2_DEFER_EPI) for the persistent single-issuer layout.
+  static constexpr bool DEFER = FA2_DEFER_EPI != 0 && !SPLIT && HALVES == 1 && !FA2_TWO_ISSUERS && !SEP_P;
   static constexpr int OFF_TMEM_PTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEM_PTR + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack to align the base to 1024 B
@@ -485,6 +499,29 @@ __device__ __forceinline__ bool next_unit(const KArgs& a, int& slot, Unit& u) {
   return false;
 }
 
+// Paged K/V: page indices of one sequence's block-table row for the TMA producer. Holds the page
+// slot in use and the one after it; looking up a new slot starts the load of the next entry, which
+// is used (and waited for) only when the producer reaches that slot.
+struct PageCache {
+  int cur_pi, cur_page, next_pi, next_page;
+  __device__ __forceinline__ void reset() { cur_pi = next_pi = -1; }
+  // Page of slot pi of `bt`, or -1 (loads zeros) for slots past the sequence's last page.
+  __device__ __forceinline__ int page(const int* bt, int pi, int pages_used) {
+    if (pi >= pages_used) return -1;
+    if (pi != cur_pi) {
+      if (pi == next_pi) {
+        cur_page = next_page;
+      } else {
+        cur_page = __ldg(bt + pi);
+      }
+      cur_pi = pi;
+      next_pi = pi + 1;
+      next_page = next_pi < pages_used ? __ldg(bt + next_pi) : -1;
+    }
+    return cur_page;
+  }
+};
+
 // ---------------------------------------------------------------- softmax helpers
 
 // Max of 64 scores (two 32-column chunks) with four independent 3-input max chains.
@@ -636,6 +673,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     for (int t = 0; t < 2; ++t) {
       mbar_init(bar(C::B_S_EMPTY + t), BM);  // every softmax thread of the tile
       mbar_init(bar(C::B_P_EMPTY + t), 1);   // the MMA thread's commit
+      mbar_init(bar(C::B_O_EMPTY + t), BM);  // every softmax thread of the tile
     }
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(C::B_KV_FULL + s), 1);
@@ -685,9 +723,12 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       if (a.gate != nullptr) ok = flag_wait(a.gate, a.timeout, a.err);
       int i = 0;  // K/V tiles issued into the ring, over all units
       int slot = 0;
+      PageCache page_a, page_b;  // two K/V streams in dual mode; named, so they stay in registers
       for (int n = 0; ok; ++n) {
         Unit u;
         if (!next_unit<CAUSAL, VARLEN>(a, slot, u)) break;
+        page_a.reset();
+        page_b.reset();
         // Q_t's buffer is free once the last QK GEMM of tile t of the previous unit retired.
         if (n > 0 && !mbar_wait(bar(C::B_Q_EMPTY + 0), static_cast<uint32_t>(n - 1) & 1u, a.timeout, a.err)) {
           ok = false;
@@ -735,9 +776,13 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             const int pos = kv_tile * BN;
             const int pages_used = (u.n_kv + a.page_size - 1) / a.page_size;
             const int boxes = a.page_size >= BN ? 1 : BN / a.page_size;
+            // Page lookups go through a small cache per K/V stream (two in dual mode): the page
+            // in use and the table entry after it, fetched as soon as the current one is known,
+            // so its load overlaps the ring waits instead of stalling the next tile's issue.
+            const bool stream_b = dual && kv_tile >= u.j0b;
             for (int sub = 0; sub < boxes; ++sub) {
               const int pi = pos / a.page_size + sub;
-              const int page = pi < pages_used ? __ldg(bt + pi) : -1;
+              const int page = stream_b ? page_b.page(bt, pi, pages_used) : page_a.page(bt, pi, pages_used);
               const int row = a.page_size >= BN ? pos % a.page_size : 0;
 #pragma unroll
               for (int c = 0; c < C::CHUNKS; ++c) {
@@ -1011,7 +1056,14 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
               // The QK issued below is its unit's last one for tile t: Q_t may be reloaded after it.
               const bool qk_final = last ? (has_next && nx.J == 1) : (j + 2 == u.J);
               const uint32_t pph = static_cast<uint32_t>(g + j) & 1u;
-              if (!kv_wait(iv) || !pv_tile(0, sv, j > 0, pph)) { ok = false; break; }
+              // DEFER: the unit's first PV overwrites O_t; the softmax warps must have read the
+              // previous unit's O_t (they do so during this unit's first step).
+              const bool o_wait = C::DEFER && j == 0 && n > 0;
+              const uint32_t oph = static_cast<uint32_t>(n - 1) & 1u;
+              if (!kv_wait(iv) || (o_wait && !mwait(C::B_O_EMPTY + 0, oph)) || !pv_tile(0, sv, j > 0, pph)) {
+                ok = false;
+                break;
+              }
               if (last) mma_commit(bar(C::B_O_FULL + 0));
               if (more) {
                 if ((last && !mwait(C::B_Q + 0, qph_next)) || !kv_wait(ik)) { ok = false; break; }
@@ -1020,7 +1072,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 mma_commit(bar(C::B_S_FULL + 0));
                 if (qk_final) mma_commit(bar(C::B_Q_EMPTY + 0));
               }
-              if (!pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
+              if ((o_wait && !mwait(C::B_O_EMPTY + 1, oph)) || !pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
               mma_commit(bar(C::B_KV_EMPTY + sv));
               if (last) mma_commit(bar(C::B_O_FULL + 1));
               if (more) {
@@ -1105,6 +1157,134 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     auto seq_done = [&]() {
       if constexpr (FA2_SEQ_EXP != 0) mbar_arrive(bar(C::B_SEQ + t * 4 + q));
     };
+    // -------------------------------------------------------------- epilogue
+    // O_t / l of unit eu (the en-th unit of this CTA) to its output: wait for its last PV, read
+    // O_t from TMEM, scale, convert and store. false when a bounded wait expired.
+    auto epilogue = [&](const Unit& eu, int en, float el, float em) -> bool {
+      (void)em;
+      const int e_row0 = eu.row0 + (dual ? 0 : t * BM);
+      {
+        bool w = mbar_wait(bar(C::B_O_FULL + t), static_cast<uint32_t>(en) & 1u, a.timeout, a.err);
+        if (!__all_sync(0xffffffffu, w)) return false;
+      }
+      tc_fence_after();
+      constexpr int EC = C::EPI_COLS / 32;  // 32-column chunks of O this warp writes
+      uint32_t o[EC][32];
+      auto load_o = [&]() {
+#pragma unroll
+        for (int c = 0; c < EC; ++c) tmem_ld32(tO + epi_c0 + c * 32, o[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < EC; ++c) reg_fence32(o[c]);
+      };
+      // Every warp writes O (ALL_EPI): its O columns are read before the row-sum exchange, whose
+      // column at D = 128 is the first of them. Otherwise (D = 64, two warps a row) the writing
+      // warp reads them after it, where it uses them.
+      if constexpr (ALL_EPI) load_o();
+      if constexpr (C::DEFER) {
+        // O_t is in registers: the next unit's first PV may overwrite it.
+        tc_fence_before();
+        mbar_arrive(bar(C::B_O_EMPTY + t));
+      }
+      float l_row = el;
+      if constexpr (HALVES == 2) {
+        // The row sum is the two partial sums, the first warp's first in both warps.
+        float l_other;
+        if (!exchange(tmem + lane_addr + C::tmem_lx(t, h), tmem + lane_addr + C::tmem_lx(t, h ^ 1), el, l_other)) {
+          return false;
+        }
+        l_row = (h == 0) ? el + l_other : l_other + el;
+      }
+      if (epi) {
+        if constexpr (!ALL_EPI) load_o();
+        if constexpr (SPLIT) {
+          // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
+          // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
+          const bool has = (l_row > 0.0f);
+          const float inv_l = has ? 1.0f / l_row : 0.0f;
+          const int split_idx = dual ? 2 * static_cast<int>(blockIdx.z) + t : static_cast<int>(blockIdx.z);
+          const int64_t slot = (static_cast<int64_t>(split_idx) * gridDim.x + eu.x) * a.rows_pad + e_row0 + r;
+          float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D + epi_c0);
+#pragma unroll
+          for (int c = 0; c < EC; ++c) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              dst[c * 8 + v] = make_float4(__uint_as_float(o[c][4 * v]) * inv_l, __uint_as_float(o[c][4 * v + 1]) * inv_l,
+                                           __uint_as_float(o[c][4 * v + 2]) * inv_l, __uint_as_float(o[c][4 * v + 3]) * inv_l);
+            }
+          }
+          if (h == 0) a.lse_part[slot] = has ? em + log2f(l_row) : -INFINITY;
+        } else {
+          // O / l in the input dtype, 64 columns at a time through this warp's staging slot and
+          // one TMA store per chunk. Lane 0 issued every store from the slot, so it alone waits
+          // for the slot to have been read before it is rewritten (the next chunk's conversion
+          // overlaps the read).
+          constexpr int ECH = C::EPI_COLS / 64;  // 64-column chunks
+          // A row that saw no key at all (a variable-length sequence without keys, bottom-right
+          // rows before the first key) has l == 0 and gets zeros.
+          const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
+          const uint64_t inv2 = f2_pack(inv_l, inv_l);
+          const int R0 = e_row0 + q * 32;  // first row of this warp
+          const int pos0 = R0 >> a.pack_shift;
+          const int h0 = eu.hq0 + (R0 & (a.pack - 1));
+          // The warp's O box covers 32 / min(PACK, 32) positions. In a variable-length batch a box
+          // that reaches past its sequence's last position would overwrite the next sequence's
+          // rows (the tensor map only clips at the end of the token axis), so such a box is
+          // written row by row from registers instead.
+          const bool rowwise = VARLEN && a.cu_q != nullptr && pos0 + (32 >> min(a.pack_shift, 5)) > eu.n_q;
+          const int my_pos = (R0 + lane) >> a.pack_shift;
+          uint16_t* my_row = static_cast<uint16_t*>(a.o) + static_cast<int64_t>(eu.q0 + my_pos) * a.on +
+                             static_cast<int64_t>(eu.hq0 + ((R0 + lane) & (a.pack - 1))) * a.oh + epi_c0;
+          const bool my_valid = my_pos < eu.n_q;
+#pragma unroll
+          for (int ch = 0; ch < ECH; ++ch) {
+            const uint32_t slot = so + (FA2_STG_FULL ? ch * C::STG_SLOT_BYTES : 0);
+            if (!FA2_STG_FULL || ch == 0) {
+              if (lane == 0) bulk_wait_read();  // the slot's previous stores have read it
+              __syncwarp();
+            }
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              // columns ch * 64 + 8 v .. + 8 of this warp's share, as four packed pairs
+              const uint32_t* src = o[2 * ch + (v >> 2)];
+              uint32_t w4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int e = (v & 3) * 8 + 2 * i;
+                float x0, x1;
+                f2_unpack(f2_mul(f2_pack(__uint_as_float(src[e]), __uint_as_float(src[e + 1])), inv2), x0, x1);
+                w4[i] = cvt_pack2<BF16>(x0, x1);
+              }
+              if (rowwise) {
+                if (my_valid) *reinterpret_cast<uint4*>(my_row + ch * 64 + v * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+              } else {
+                st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
+                             w4[0], w4[1], w4[2], w4[3]);
+              }
+            }
+            if (!rowwise && (!FA2_STG_FULL || ch == ECH - 1)) {
+              fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0 && pos0 < eu.n_q) {
+#pragma unroll
+                for (int c2 = (FA2_STG_FULL ? 0 : ch); c2 <= ch; ++c2) {
+                  tma_store_4d(&tmO, so + (FA2_STG_FULL ? c2 * C::STG_SLOT_BYTES : 0), epi_c0 + c2 * 64, h0,
+                               eu.q0 + pos0, eu.tb);
+                }
+                bulk_commit();
+              }
+            }
+          }
+        }
+      }
+      return true;
+    };
+    // DEFER: the unit whose output is still to be written (by the next unit's first step).
+    Unit pend;
+    int pend_n = 0;
+    float pend_l = 0.0f;
+    bool pending = false;
+
     Unit u;
     int slot = 0;
     bool have = next_unit<CAUSAL, VARLEN>(a, slot, u);
@@ -1212,6 +1392,10 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           float sl0, sl1;
           f2_unpack(acc01, sl0, sl1);
           l = l * alpha + (sl0 + sl1);
+          if (C::DEFER && pending && j == 0) {  // (not reached: the speculative path needs j > 0)
+            if (!epilogue(pend, pend_n, pend_l, 0.0f)) { ok = false; break; }
+            pending = false;
+          }
           continue;
         }
         if (masked) {
@@ -1289,126 +1473,29 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         float sl0, sl1;
         f2_unpack(acc01, sl0, sl1);
         l = l * alpha + (sl0 + sl1);
+        if (C::DEFER && pending && j == 0) {
+          // The previous unit's output, in the gap before this unit's S_t(1) (or the next unit).
+          if (!epilogue(pend, pend_n, pend_l, 0.0f)) { ok = false; break; }
+          pending = false;
+        }
       }
       if (!ok) break;
       g += J;
       // The next unit, decoded while PV(t, J - 1) runs.
       Unit nu;
       have = next_unit<CAUSAL, VARLEN>(a, slot, nu);
-
-      // -------------------------------------------------------------- epilogue
-      {
-        bool w = mbar_wait(bar(C::B_O_FULL + t), static_cast<uint32_t>(n) & 1u, a.timeout, a.err);
-        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
-      }
-      tc_fence_after();
-      constexpr int EC = C::EPI_COLS / 32;  // 32-column chunks of O this warp writes
-      uint32_t o[EC][32];
-      auto load_o = [&]() {
-#pragma unroll
-        for (int c = 0; c < EC; ++c) tmem_ld32(tO + epi_c0 + c * 32, o[c]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c = 0; c < EC; ++c) reg_fence32(o[c]);
-      };
-      // Every warp writes O (ALL_EPI): its O columns are read before the row-sum exchange, whose
-      // column at D = 128 is the first of them. Otherwise (D = 64, two warps a row) the writing
-      // warp reads them after it, where it uses them.
-      if constexpr (ALL_EPI) load_o();
-      float l_row = l;
-      if constexpr (HALVES == 2) {
-        // The row sum is the two partial sums, the first warp's first in both warps.
-        float l_other;
-        if (!exchange(tmem + lane_addr + C::tmem_lx(t, h), tmem + lane_addr + C::tmem_lx(t, h ^ 1), l, l_other)) {
-          ok = false;
-          break;
-        }
-        l_row = (h == 0) ? l + l_other : l_other + l;
-      }
-      if (epi) {
-        if constexpr (!ALL_EPI) load_o();
-        if constexpr (SPLIT) {
-          // Split-KV partial: O / l in fp32 and the row's log2-sum-exp (in qk_scale units), one
-          // row per thread, for the combine kernel. Rows that saw no visible column get 0, -inf.
-          const bool has = (l_row > 0.0f);
-          const float inv_l = has ? 1.0f / l_row : 0.0f;
-          const int split_idx = dual ? 2 * static_cast<int>(blockIdx.z) + t : static_cast<int>(blockIdx.z);
-          const int64_t slot = (static_cast<int64_t>(split_idx) * gridDim.x + u.x) * a.rows_pad + tile_row0 + r;
-          float4* dst = reinterpret_cast<float4*>(a.o_part + slot * D + epi_c0);
-#pragma unroll
-          for (int c = 0; c < EC; ++c) {
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              dst[c * 8 + v] = make_float4(__uint_as_float(o[c][4 * v]) * inv_l, __uint_as_float(o[c][4 * v + 1]) * inv_l,
-                                           __uint_as_float(o[c][4 * v + 2]) * inv_l, __uint_as_float(o[c][4 * v + 3]) * inv_l);
-            }
-          }
-          if (h == 0) a.lse_part[slot] = has ? m_use + log2f(l_row) : -INFINITY;
-        } else {
-          // O / l in the input dtype, 64 columns at a time through this warp's staging slot and
-          // one TMA store per chunk. Lane 0 issued every store from the slot, so it alone waits
-          // for the slot to have been read before it is rewritten (the next chunk's conversion
-          // overlaps the read).
-          constexpr int ECH = C::EPI_COLS / 64;  // 64-column chunks
-          // A row that saw no key at all (a variable-length sequence without keys, bottom-right
-          // rows before the first key) has l == 0 and gets zeros.
-          const float inv_l = l_row > 0.0f ? 1.0f / l_row : 0.0f;
-          const uint64_t inv2 = f2_pack(inv_l, inv_l);
-          const int R0 = tile_row0 + q * 32;  // first row of this warp
-          const int pos0 = R0 >> a.pack_shift;
-          const int h0 = u.hq0 + (R0 & (a.pack - 1));
-          // The warp's O box covers 32 / min(PACK, 32) positions. In a variable-length batch a box
-          // that reaches past its sequence's last position would overwrite the next sequence's
-          // rows (the tensor map only clips at the end of the token axis), so such a box is
-          // written row by row from registers instead.
-          const bool rowwise = VARLEN && a.cu_q != nullptr && pos0 + (32 >> min(a.pack_shift, 5)) > u.n_q;
-          const int my_pos = (R0 + lane) >> a.pack_shift;
-          uint16_t* my_row = static_cast<uint16_t*>(a.o) + static_cast<int64_t>(u.q0 + my_pos) * a.on +
-                             static_cast<int64_t>(u.hq0 + ((R0 + lane) & (a.pack - 1))) * a.oh + epi_c0;
-          const bool my_valid = my_pos < u.n_q;
-#pragma unroll
-          for (int ch = 0; ch < ECH; ++ch) {
-            const uint32_t slot = so + (FA2_STG_FULL ? ch * C::STG_SLOT_BYTES : 0);
-            if (!FA2_STG_FULL || ch == 0) {
-              if (lane == 0) bulk_wait_read();  // the slot's previous stores have read it
-              __syncwarp();
-            }
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              // columns ch * 64 + 8 v .. + 8 of this warp's share, as four packed pairs
-              const uint32_t* src = o[2 * ch + (v >> 2)];
-              uint32_t w4[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int e = (v & 3) * 8 + 2 * i;
-                float x0, x1;
-                f2_unpack(f2_mul(f2_pack(__uint_as_float(src[e]), __uint_as_float(src[e + 1])), inv2), x0, x1);
-                w4[i] = cvt_pack2<BF16>(x0, x1);
-              }
-              if (rowwise) {
-                if (my_valid) *reinterpret_cast<uint4*>(my_row + ch * 64 + v * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-              } else {
-                st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
-                             w4[0], w4[1], w4[2], w4[3]);
-              }
-            }
-            if (!rowwise && (!FA2_STG_FULL || ch == ECH - 1)) {
-              fence_proxy_async_smem();
-              __syncwarp();
-              if (lane == 0 && pos0 < u.n_q) {
-#pragma unroll
-                for (int c2 = (FA2_STG_FULL ? 0 : ch); c2 <= ch; ++c2) {
-                  tma_store_4d(&tmO, so + (FA2_STG_FULL ? c2 * C::STG_SLOT_BYTES : 0), epi_c0 + c2 * 64, h0,
-                               u.q0 + pos0, u.tb);
-                }
-                bulk_commit();
-              }
-            }
-          }
-        }
+      if constexpr (C::DEFER) {
+        // This unit's output is written during the next unit's first step (or after the loop).
+        pend = u;
+        pend_n = n;
+        pend_l = l;
+        pending = true;
+      } else {
+        if (!epilogue(u, n, l, m_use)) { ok = false; break; }
       }
       u = nu;
     }
+    if (ok && pending && !epilogue(pend, pend_n, pend_l, 0.0f)) ok = false;
     if (lane == 0) bulk_wait_all();  // the last stores have read the slot and written O
   } else {
     // The spare warps of the MMA/TMA warpgroup (warp 10 also issues with two issuers).
