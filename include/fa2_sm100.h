@@ -93,7 +93,7 @@ typedef struct Fa2FwdParams {
   int32_t heads_kv;
   int32_t seqlen_q;
   int32_t seqlen_kv;
-  int32_t head_dim;  /* 64 or 128 */
+  int32_t head_dim;  /* 16, 32, 64 or 128 (16 and 32 run on the 64 build, read and written in place) */
   int32_t dtype;     /* Fa2DType */
   int32_t causal;    /* causal mask, aligned as causal_align says (per sequence when variable-length) */
   int32_t pack_gqa;  /* 1: a GQA group's query heads share one 128-row tile */
@@ -171,7 +171,8 @@ FA2_API int fa2_fwd_sm100_noalloc(const Fa2FwdParams* p, void* stream);
 
 /* Static description of the compiled kernel family (fa2/kernel.py:186-195 analogue):
  * fills BLOCK_M, BLOCK_N, threads per CTA, K/V pipeline stages and dynamic shared memory
- * bytes for `head_dim`. Returns FA2_OK or FA2_ERR_HEAD_DIM. Host only. */
+ * bytes for `head_dim` (16 and 32 report the 64 build that serves them). Returns FA2_OK or
+ * FA2_ERR_HEAD_DIM. Host only. */
 FA2_API int fa2_fwd_sm100_config(int32_t head_dim, int32_t* block_m, int32_t* block_n,
                          int32_t* threads, int32_t* stages, int32_t* smem_bytes);
 

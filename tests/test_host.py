@@ -38,6 +38,7 @@ def test_abi_version_and_struct_size():
 def test_config_entry_point():
     assert _lib.config(128)[:2] == (128, 128)
     assert _lib.config(64)[:2] == (128, 128)
+    assert _lib.config(16) == _lib.config(32) == _lib.config(64)  # served by the 64 build
     with pytest.raises(_lib.Fa2Error):
         _lib.config(96)
     bm, bn, warps, stages = _default_config(128, True)
@@ -73,6 +74,8 @@ def test_check_accepts_valid():
     assert _lib.check(params(causal=0, Nq=23, Nkv=70, D=64)) == _lib.FA2_OK
     assert _lib.check(params(Nq=0, Nkv=0, causal=0)) == _lib.FA2_ERR_SHAPE  # N_kv must be >= 1
     assert _lib.check(params(Nq=0, Nkv=5, causal=0)) == _lib.FA2_OK          # empty query is a no-op
+    assert _lib.check(params(D=16)) == _lib.FA2_OK                            # 16 / 32 in place
+    assert _lib.check(params(D=32, pack_gqa=1)) == _lib.FA2_OK
 
 
 @pytest.mark.parametrize("kw,status", [
@@ -82,6 +85,7 @@ def test_check_accepts_valid():
     (dict(Nq=64, Nkv=100), _lib.FA2_ERR_SHAPE),          # causal needs N_q == N_kv (fa2/kernel.py:225-228)
     (dict(dtype=7), _lib.FA2_ERR_DTYPE),
     (dict(D=96), _lib.FA2_ERR_HEAD_DIM),
+    (dict(D=8), _lib.FA2_ERR_HEAD_DIM),
     (dict(Hq=6, Hkv=4), _lib.FA2_ERR_GQA),                # fa2/kernel.py:223
     (dict(Hq=6, Hkv=2, pack_gqa=1), _lib.FA2_ERR_PACK),   # group 3 does not divide 128
     (dict(qk_scale=-0.1), _lib.FA2_ERR_SCALE),            # fa2/kernel.py:242-243
@@ -183,6 +187,9 @@ def test_workspace_validation_and_size():
     p4 = params(causal=0, Nq=4, Nkv=4096, num_splits=4, workspace=0x10000, workspace_bytes=need)
     assert _lib.check(p4) == _lib.FA2_OK
     assert _lib.workspace_bytes(params()) == 0                           # no split, no workspace
+    # head_dim 16 / 32: the partials have the 64 build's columns
+    d16 = params(causal=0, Nq=4, Nkv=4096, num_splits=4, D=16)
+    assert _lib.workspace_bytes(d16) == 4 * (2 * 8) * 256 * 65 * 4 + 256
 
 
 def test_auto_num_splits():

@@ -135,9 +135,60 @@ def test_kernel_unaligned_strides_take_a_layout_copy():
     check_against_oracle(q, k, v, causal=True)
 
 
+# head_dim 16 and 32 run on the D = 64 build in place: the tensor maps are head_dim wide, TMA
+# fills the rest of each 64-column box with zeros and clips the output stores.
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("D", [16, 32])
-def test_kernel_small_head_dims(D):
-    check_against_oracle(*make_cuda_qkv(2, 4, 2, 100, 100, D, torch.float16), causal=True)
+def test_kernel_small_head_dims(D, dtype, causal):
+    check_against_oracle(*make_cuda_qkv(2, 4, 2, 300, 300, D, dtype), causal=causal)
+
+
+@pytest.mark.parametrize("D", [16, 32])
+def test_small_head_dims_full_tiles_and_packing(D):
+    """Long enough that unmasked tiles (the FMA-pipe exp2 pairs) run; packed == unpacked."""
+    q, k, v = make_cuda_qkv(2, 32, 8, 1000, 1000, D, torch.bfloat16, seed=1)
+    assert torch.equal(attention(q, k, v, pack_gqa=True), attention(q, k, v, pack_gqa=False))
+    check_against_oracle(q, k, v, causal=True)
+    check_against_oracle(*make_cuda_qkv(1, 8, 8, 2048, 2048, D, torch.float16, seed=2), causal=False)
+
+
+@pytest.mark.parametrize("D", [16, 32])
+@pytest.mark.parametrize("num_splits", [2, 5])
+def test_small_head_dims_split_kv(D, num_splits):
+    """Split-KV: the fp32 partials keep 64 columns, the merge writes head_dim of them."""
+    check_against_oracle(*make_cuda_qkv(2, 16, 4, 3, 5000, D, torch.bfloat16, seed=3), causal=False,
+                         num_splits=num_splits)
+    check_against_oracle(*make_cuda_qkv(2, 4, 4, 100, 3000, D, torch.float16, seed=4), causal=False,
+                         num_splits=num_splits)
+
+
+@pytest.mark.parametrize("D", [16, 32])
+@pytest.mark.parametrize("num_splits", [1, 4])
+def test_small_head_dim_writes_only_its_columns(D, num_splits):
+    """Through the C ABI, with q/k/v/o as the first D columns of 64-column rows: the output
+    columns past D (pre-filled with NaN) are never written, by the clipped TMA stores or by the
+    merge kernel, and every column below D is."""
+    B, H, N = 2, 8, 333 if num_splits == 1 else 5
+    base = [t for t in make_cuda_qkv(B, H, H, N, 2000 if num_splits > 1 else N, 64, torch.bfloat16, seed=5)]
+    q, k, v = (t[..., :D] for t in base)
+    wide = torch.full_like(base[0], float("nan"))
+    out = wide[..., :D]
+    p = _lib.make_params(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                         q.stride(), k.stride(), v.stride(), out.stride(),
+                         B, H, H, N, k.shape[2], D, _lib.FA2_DTYPE_BF16, 0, 0,
+                         1.0 / math.sqrt(D) * 1.4426950408889634, num_splits=num_splits)
+    ws = None
+    if num_splits > 1:
+        nbytes = _lib.workspace_bytes(p)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
+    assert _lib.launch(p, torch.cuda.current_stream().cuda_stream) == _lib.FA2_OK
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert torch.isnan(wide[..., D:]).all()
+    assert torch.equal(out, attention(q.contiguous(), k.contiguous(), v.contiguous(), causal=False,
+                                      num_splits=num_splits))
 
 
 # ------------------------------------------------------------------- GQA head packing

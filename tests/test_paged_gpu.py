@@ -93,6 +93,14 @@ def test_paged_split_kv_fp16_d64(num_splits):
     check_paged(q, k, v, bt, sl, causal=True, num_splits=num_splits)
 
 
+@pytest.mark.parametrize("D", [16, 32])
+def test_paged_small_head_dims(D):
+    """head_dim 16 / 32 pages read in place by the D = 64 build (zero-filled box columns)."""
+    q, k, v, bt, sl = paged_inputs(3, 8, 2, 5, [3000, 77, 1024], 64, D, torch.bfloat16, seed=7)
+    check_paged(q, k, v, bt, sl, causal=True, num_splits=1)
+    check_paged(q, k, v, bt, sl, causal=True, num_splits=4)
+
+
 def test_paged_unequal_lengths_top_left_and_empty():
     """Per-sequence top-left masks, a sequence without keys (zeros), a one-key sequence."""
     q, k, v, bt, sl = paged_inputs(4, 8, 8, 64, [0, 1, 700, 64], 64, 128, torch.bfloat16, seed=3)

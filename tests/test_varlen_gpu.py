@@ -144,8 +144,12 @@ def test_varlen_every_row_written_and_nothing_else():
         assert torch.equal(alone, out[c[b]:c[b + 1]])
 
 
-def test_varlen_small_head_dim():
-    check_varlen([50, 200], [50, 200], 4, 2, 32, torch.float16, True)
+@pytest.mark.parametrize("D", [16, 32])
+def test_varlen_small_head_dim(D):
+    """The rows of a box that crosses a sequence end are written from registers: only the
+    head_dim columns."""
+    check_varlen([50, 200, 3, 700], [50, 200, 3, 700], 4, 2, D, torch.float16, True)
+    check_varlen([50, 200, 3, 700], [50, 200, 3, 700], 8, 8, D, torch.bfloat16, False)
 
 
 def test_varlen_longer_than_declared_is_reported():

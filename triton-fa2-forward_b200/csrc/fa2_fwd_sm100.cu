@@ -348,6 +348,10 @@ struct KArgs {
   int bt_stride, page_size;
   void* o;                              // output base and element strides (h, n): used for the
   int64_t oh, on;                       // rows of a variable-length sequence's last O box
+  // Columns of the caller's head dimension (16 or 32 on the D = 64 build, else D). The tensor
+  // maps have this extent, so TMA loads fill the columns past it with zeros (they add nothing to
+  // Q K^T and make zero O columns) and TMA stores clip them; register stores check it.
+  int d_real;
   int pack_shift;                       // pack == 1 << pack_shift (pack divides 128)
   FastDiv div_xblocks, div_hblocks, div_group, div_mblocks;
   float qk_scale;
@@ -1256,7 +1260,9 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
                 w4[i] = cvt_pack2<BF16>(x0, x1);
               }
               if (rowwise) {
-                if (my_valid) *reinterpret_cast<uint4*>(my_row + ch * 64 + v * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                if (my_valid && epi_c0 + ch * 64 + v * 8 < a.d_real) {
+                  *reinterpret_cast<uint4*>(my_row + ch * 64 + v * 8) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                }
               } else {
                 st_shared_v4(slot + lane * 128 + ((static_cast<uint32_t>(v) ^ static_cast<uint32_t>(lane & 7)) << 4),
                              w4[0], w4[1], w4[2], w4[3]);
@@ -1521,6 +1527,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
 struct CombineArgs {
   int n_q, n_kv, pack, pack_shift, hblocks, rows_pad, num_splits, split_tiles, causal_off, xblocks;
   int bottom_right;
+  int d_real;             // output columns (the caller's head dimension, <= D)
   const int* seqlens_kv;  // paged K/V: keys per sequence (n_kv and causal_off per batch); else nullptr
   int64_t ob, oh, on;     // output element strides (b, h, n); d stride is 1
 };
@@ -1563,6 +1570,7 @@ fa2_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l
       for (int i = 0; i < PER; ++i) acc[i] = fmaf(w, src[i], acc[i]);
     }
     const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+    if (lane * PER >= c.d_real) continue;  // columns past the caller's head dimension
     uint16_t* dst = reinterpret_cast<uint16_t*>(out) + b * c.ob + h * c.oh + pos * c.on + lane * PER;
 #pragma unroll
     for (int i = 0; i < PER; i += 2) {
@@ -1633,6 +1641,11 @@ int num_sms(int device) {
   return cache[device];
 }
 
+// Head dimension of the compiled kernel that serves a caller's head_dim: 16 and 32 run on the
+// D = 64 build (their tensor maps are head_dim wide; TMA fills the rest of a 64-column box with
+// zeros), 64 and 128 on their own.
+int kernel_d(int head_dim) { return head_dim <= 64 ? 64 : 128; }
+
 struct SplitPlan {
   int num_splits = 1, split_tiles = 0, rows_pad = 0, xblocks = 0, dual = 0, grid_z = 1;
   int64_t bytes = 0;
@@ -1661,7 +1674,7 @@ SplitPlan plan_splits(const Fa2FwdParams* p) {
   sp.split_tiles = (j_max + sp.num_splits - 1) / sp.num_splits;
   sp.rows_pad = mblocks * 256;
   sp.xblocks = p->batch * (p->heads_q / pack);
-  sp.bytes = static_cast<int64_t>(sp.num_splits) * sp.xblocks * sp.rows_pad * (p->head_dim + 1) * 4 + 256;
+  sp.bytes = static_cast<int64_t>(sp.num_splits) * sp.xblocks * sp.rows_pad * (kernel_d(p->head_dim) + 1) * 4 + 256;
   return sp;
 }
 
@@ -1693,7 +1706,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   CUtensorMap tmQ, tmK, tmV, tmO;
   // Variable-length batches: one packed token axis (b extent 1) of total_q / total_kv rows.
   const bool varlen = p->cu_seqlens_q != nullptr;
-  const int64_t qdims[4] = {D, p->heads_q, varlen ? p->total_q : p->seqlen_q, varlen ? 1 : p->batch};
+  const int64_t qdims[4] = {p->head_dim, p->heads_q, varlen ? p->total_q : p->seqlen_q, varlen ? 1 : p->batch};
   const int64_t qstr[4] = {1, p->q_stride[1], p->q_stride[2], p->q_stride[0]};
   const int64_t ostr[4] = {1, p->o_stride[1], p->o_stride[2], p->o_stride[0]};
   const uint32_t gh_q = static_cast<uint32_t>(pack);           // heads per 128-row Q box
@@ -1703,7 +1716,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   // K / V: dims (d, n, h, b), 128-row boxes of one head.
   // Paged K/V: dims (d, row in page, h, page); otherwise (d, n, h, b).
   const bool paged = p->block_table != nullptr;
-  const int64_t kdims[4] = {D, paged ? p->page_size : (varlen ? p->total_kv : p->seqlen_kv), p->heads_kv,
+  const int64_t kdims[4] = {p->head_dim, paged ? p->page_size : (varlen ? p->total_kv : p->seqlen_kv), p->heads_kv,
                             paged ? p->num_pages : (varlen ? 1 : p->batch)};
   const int64_t kstr[4] = {1, p->k_stride[2], p->k_stride[1], p->k_stride[0]};
   const int64_t vstr[4] = {1, p->v_stride[2], p->v_stride[1], p->v_stride[0]};
@@ -1734,6 +1747,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   ka.o = p->o;
   ka.oh = p->o_stride[1];
   ka.on = p->o_stride[2];
+  ka.d_real = p->head_dim;
   ka.qk_scale = p->qk_scale;
   ka.err = p->err_flag;
   ka.gate = p->gate;
@@ -1784,6 +1798,7 @@ int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
     ca.split_tiles = sp.split_tiles;
     ca.causal_off = ka.causal_off;
     ca.bottom_right = ka.bottom_right;
+    ca.d_real = p->head_dim;
     ca.seqlens_kv = paged ? p->seqlens_kv : nullptr;
     ca.xblocks = sp.xblocks;
     ca.ob = p->o_stride[0];
@@ -1831,7 +1846,7 @@ const char* fa2_sm100_strerror(int status) {
     case FA2_ERR_NULL: return "a required pointer is NULL";
     case FA2_ERR_SHAPE: return "invalid shape (sizes, batch/head_dim mismatch, causal top-left with N_q != N_kv, or causal bottom-right with N_q > N_kv)";
     case FA2_ERR_DTYPE: return "dtype must be fp16 or bf16";
-    case FA2_ERR_HEAD_DIM: return "head_dim not supported by the compiled sm_100a kernels (64, 128)";
+    case FA2_ERR_HEAD_DIM: return "head_dim not supported by the compiled sm_100a kernels (16, 32, 64, 128)";
     case FA2_ERR_GQA: return "H_q must be divisible by H_kv";
     case FA2_ERR_PACK: return "pack_gqa needs the GQA group to divide BLOCK_M (128)";
     case FA2_ERR_SCALE: return "qk_scale must be finite and > 0";
@@ -1849,7 +1864,7 @@ const char* fa2_sm100_strerror(int status) {
 int fa2_fwd_sm100_config(int32_t head_dim, int32_t* block_m, int32_t* block_n, int32_t* threads,
                          int32_t* stages, int32_t* smem_bytes) {
   int st = 0, sm = 0;
-  if (head_dim == 64) {
+  if (head_dim == 16 || head_dim == 32 || head_dim == 64) {
     st = Cfg<64>::STAGES;
     sm = Cfg<64>::SMEM_ALLOC;
   } else if (head_dim == 128) {
@@ -1893,7 +1908,7 @@ int check_core(const Fa2FwdParams* p) {
     if (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT && p->seqlen_q > p->seqlen_kv) return FA2_ERR_SHAPE;
   }
   if (p->dtype != FA2_DTYPE_FP16 && p->dtype != FA2_DTYPE_BF16) return FA2_ERR_DTYPE;
-  if (p->head_dim != 64 && p->head_dim != 128) return FA2_ERR_HEAD_DIM;
+  if (p->head_dim != 16 && p->head_dim != 32 && p->head_dim != 64 && p->head_dim != 128) return FA2_ERR_HEAD_DIM;
   if (p->heads_q % p->heads_kv != 0) return FA2_ERR_GQA;
   const int group = p->heads_q / p->heads_kv;
   if (p->pack_gqa && (fa2::BM % group) != 0) return FA2_ERR_PACK;
@@ -1947,7 +1962,7 @@ int fa2_fwd_sm100(const Fa2FwdParams* p, void* stream) {
   if (major != 10 || minor != 0) return FA2_ERR_DEVICE;
   if (encode_fn() == nullptr) return FA2_ERR_DEVICE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return p->head_dim == 64 ? dispatch_d<64>(p, s, dev) : dispatch_d<128>(p, s, dev);
+  return kernel_d(p->head_dim) == 64 ? dispatch_d<64>(p, s, dev) : dispatch_d<128>(p, s, dev);
 }
 
 }  // extern "C"

@@ -19,8 +19,9 @@ Differences from the reference that do not change results:
     its ValueError exactly as in the reference; the others do not change the kernel.
   * Packed and unpacked runs are bit-identical (same tiles, same order, per-row decisions),
     so a group that divides the hinted block_m but not 128 simply runs unpacked.
-  * head_dim 16 and 32 run the 64 kernel on zero-padded copies (extra zero columns add
-    nothing to QK^T and produce zero output columns that are dropped).
+  * head_dim 16 and 32 run on the 64 kernel in place: its tensor maps are head_dim wide, so
+    TMA fills the rest of each 64-column box with zeros (adding nothing to QK^T) and clips the
+    stores of the zero output columns. No copies, no extra HBM traffic.
 
 Also (no counterpart in the reference, whose README lists variable-length batches and paged K/V
 out of scope):
@@ -244,13 +245,6 @@ def attention(q, k, v, causal=True, sm_scale=None, block_m=None, block_n=None,
     out = torch.empty_like(q)
     if out.numel() == 0:
         return out
-    if D < 64:
-        pad = (0, 64 - D)
-        qp, kp, vp = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
-        op = torch.empty_like(qp)
-        _run(qp, kp, vp, op, causal, pack, qk_scale, num_splits, align=align)
-        out.copy_(op[..., :D])
-        return out
     return _run(q, k, v, out, causal, pack, qk_scale, num_splits, align=align)
 
 
@@ -294,13 +288,6 @@ def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seql
         return out
     if total_k == 0 or max_seqlen_k == 0:
         return out.zero_()  # no sequence has a key: every query sees none
-    if D < 64:
-        pad = (0, 64 - D)
-        qp, kp, vp = (torch.nn.functional.pad(t, pad) for t in (q, k, v))
-        op = attention_varlen(qp, kp, vp, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, causal,
-                              sm_scale, pack_gqa, causal_align)
-        out.copy_(op[..., :D])
-        return out
     cq, ck = cu_seqlens_q.contiguous(), cu_seqlens_k.contiguous()
 
     def launch(qq, kk, vv, oo, pk):
@@ -348,7 +335,7 @@ def attention_kvcache(q, k_cache, v_cache, block_table, cache_seqlens, max_seqle
     assert q.dim() == 4 and k_cache.dim() == 4 and v_cache.shape == k_cache.shape
     B, H_q, N_q, D = q.shape
     num_pages, page_size, H_kv, Dk = k_cache.shape
-    assert Dk == D and D in (64, 128), "paged K/V needs head_dim 64 or 128"
+    assert Dk == D and D in (16, 32, 64, 128), "head_dim must be a power of two in [16, 128]"
     assert q.dtype == k_cache.dtype == v_cache.dtype and q.dtype in (torch.float16, torch.bfloat16)
     assert H_q % H_kv == 0, "GQA needs H_q divisible by H_kv"
     assert causal_align in CAUSAL_ALIGNS, f"causal_align must be one of {sorted(CAUSAL_ALIGNS)}"
