@@ -233,10 +233,12 @@ def test_profile_target_configs_cover_the_ablation():
         assert cfg in CONFIGS
 
 
-def test_row_split_layout_builds(tmp_path):
-    """The 20-warp alternative (two softmax warps per row quadrant) still compiles for sm_100a,
-    so its register and shared-memory budgets (static_asserts) and its generic softmax code stay
-    checked although the shipped library uses the 12-warp layout. Compilation only: no GPU."""
+@pytest.mark.parametrize("flag", ["-DFA2_ROW_SPLIT=2", "-DFA2_PAIR=1"])
+def test_alternative_layouts_build(tmp_path, flag):
+    """The alternatives the shipped library leaves out still compile for sm_100a, so their
+    register and shared-memory budgets (static_asserts) and code stay checked: the 20-warp layout
+    (two softmax warps per row quadrant) and the CTA-pair kernel (cta_group::2, fa2_pair_sm100.cuh).
+    Compilation only: no GPU."""
     import shutil
     import subprocess
 
@@ -245,8 +247,8 @@ def test_row_split_layout_builds(tmp_path):
     nvcc = fa2_build.nvcc_path()
     if shutil.which(nvcc) is None and not os.path.exists(nvcc):
         pytest.skip("nvcc not available")
-    out = tmp_path / "libfa2_row_split_2.so"
-    cmd = [nvcc, *fa2_build.NVCC_FLAGS, "-DFA2_ROW_SPLIT=2", "-I", fa2_build.INCLUDE, "-I", fa2_build.CSRC,
+    out = tmp_path / "libfa2_variant.so"
+    cmd = [nvcc, *fa2_build.NVCC_FLAGS, flag, "-I", fa2_build.INCLUDE, "-I", fa2_build.CSRC,
            "-o", str(out), *fa2_build.SOURCES]
     res = subprocess.run(cmd, capture_output=True, text=True)
     assert res.returncode == 0, res.stderr[-3000:]

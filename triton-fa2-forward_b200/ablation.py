@@ -48,6 +48,9 @@ Every variant computes the full attention (no work is skipped); they differ only
   ffma_pass      s * qk_scale - m for the whole row in one FMA pass before the exponentials
                  (FA2_FFMA_PASS=1) instead of fused into the per-chunk loop
   seq_exp_ffma_pass   both
+  pair           CTA pairs at D=128 (FA2_PAIR=1: fixed-length launches without split-KV of at
+                 least 1024 packed rows per head block run fa2_fwd_pair_kernel, one M = 256
+                 cta_group::2 MMA over two SMs with K/V split between them) instead of one CTA
   pack_off       (runtime) GQA head packing forced off, on the pack_tail config (the wrapper
                  packs whenever the group divides 128; the reference's rule would not pack here)
   pack_off_headline, pack_off_mqa   the same on the headline and on an MQA shape
@@ -112,6 +115,7 @@ COMPILED = {
     "row_major_noncausal": ["-DFA2_HEAD_MAJOR=0"],
     "ffma_pass": ["-DFA2_FFMA_PASS=1"],
     "seq_exp_ffma_pass": ["-DFA2_SEQ_EXP=1", "-DFA2_FFMA_PASS=1"],
+    "pair": ["-DFA2_PAIR=1"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)

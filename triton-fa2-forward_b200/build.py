@@ -21,6 +21,7 @@ SOURCES = [os.path.join(CSRC, "fa2_fwd_sm100.cu")]
 DEPENDS = SOURCES + [
     os.path.join(CSRC, "ptx_sm100.cuh"),
     os.path.join(CSRC, "exp2_poly.cuh"),
+    os.path.join(CSRC, "fa2_pair_sm100.cuh"),
     os.path.join(INCLUDE, "fa2_sm100.h"),
 ]
 

@@ -200,6 +200,19 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // 0 (shipped): P overwrites S_t, as at D = 128 (which has no TMEM left for a separate P).
 #define FA2_SEP_P_D64 0
 #endif
+#ifndef FA2_PAIR
+// 1: fixed-length D = 128 launches without split-KV of at least FA2_PAIR_MIN_ROWS packed rows per
+// (batch, head block) run on CTA pairs (fa2_pair_sm100.cuh: one M = 256 cta_group::2 MMA over two
+// SMs, K/V split between them). Same-box A/B against the single-CTA kernel: headline +0.5..2.4%,
+// pack_tail +3..5%, mha_causal -4.5..6%, MQA -1.7%, non-causal D = 128 within +-2%. Each SM then
+// moves half the K/V bytes and its MMAs run at ~64 instead of ~75-80 cycles per k-step, but every
+// hand-off waits for the slower of two SMs and the even CTA's MMA warp still slows the softmax
+// warp on its SMSP. 0 (shipped): always the single-CTA kernel.
+#define FA2_PAIR 0
+#endif
+#ifndef FA2_PAIR_MIN_ROWS
+#define FA2_PAIR_MIN_ROWS 1024
+#endif
 #ifndef FA2_HEAD_MAJOR
 // 1: without a causal mask the persistent CTAs walk the units (batch, head) slice by slice;
 // 0: row block by row block, as with a causal mask (every head's K/V in flight at once).
@@ -395,6 +408,7 @@ __host__ __device__ __forceinline__ int cta_kv_tiles(int mb, int n_q, int n_kv, 
 struct Unit {
   int x, b, hq0, hkv, row0, j0, j0b, J;
   int q0, kv0, tb, tbkv, n_q, n_kv, coff;
+  int J0;  // CTA pairs: K/V tiles of the unit's first 256 rows (<= J, which covers all 512)
 };
 
 // Unit slot n of this CTA; false when the CTA has no n-th slot. J == 0: the unit is empty (a
@@ -1582,6 +1596,10 @@ fa2_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ l
 
 }  // namespace fa2
 
+#if FA2_PAIR != 0
+#include "fa2_pair_sm100.cuh"
+#endif
+
 // =============================================================================== host
 
 namespace {
@@ -1678,9 +1696,108 @@ SplitPlan plan_splits(const Fa2FwdParams* p) {
   return sp;
 }
 
+#if FA2_PAIR != 0
+// CTA-pair launch (fa2_fwd_pair_kernel): clusters of two CTAs, persistent over 512-row units.
+template <bool CAUSAL, bool BF16>
+int launch_pair(const Fa2FwdParams* p, cudaStream_t stream, int device) {
+  using PC = fa2::PairCfg;
+  auto kern = fa2::fa2_fwd_pair_kernel<CAUSAL, BF16>;
+  static bool attr_done[kMaxDevices] = {};
+  static int max_clusters[kMaxDevices] = {};
+  if (device < 0 || device >= kMaxDevices) return FA2_ERR_DEVICE;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(fa2::NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PC::SMEM_ALLOC;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!attr_done[device]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PC::SMEM_ALLOC) != cudaSuccess) {
+      return FA2_ERR_LAUNCH;
+    }
+    const int sms = num_sms(device);
+    if (sms < 2) return FA2_ERR_DEVICE;
+    cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
+    int mc = 0;
+    if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) != cudaSuccess || mc < 1) return FA2_ERR_LAUNCH;
+    max_clusters[device] = mc;
+    attr_done[device] = true;
+  }
+  const int group = p->heads_q / p->heads_kv;
+  const int pack = p->pack_gqa ? group : 1;
+  CUtensorMap tmQ, tmK, tmV, tmO;
+  const int64_t qdims[4] = {p->head_dim, p->heads_q, p->seqlen_q, p->batch};
+  const int64_t qstr[4] = {1, p->q_stride[1], p->q_stride[2], p->q_stride[0]};
+  const int64_t ostr[4] = {1, p->o_stride[1], p->o_stride[2], p->o_stride[0]};
+  const uint32_t gh_q = static_cast<uint32_t>(pack);
+  const uint32_t qbox[4] = {64, gh_q, 128u / gh_q, 1};
+  const uint32_t gh_o = static_cast<uint32_t>(pack < 32 ? pack : 32);
+  const uint32_t obox[4] = {64, gh_o, 32u / gh_o, 1};
+  const int64_t kdims[4] = {p->head_dim, p->seqlen_kv, p->heads_kv, p->batch};
+  const int64_t kstr[4] = {1, p->k_stride[2], p->k_stride[1], p->k_stride[0]};
+  const int64_t vstr[4] = {1, p->v_stride[2], p->v_stride[1], p->v_stride[0]};
+  const uint32_t kbox[4] = {64, 64, 1, 1};   // half a K tile: 64 keys
+  const uint32_t vbox[4] = {64, 128, 1, 1};  // half a V tile: 64 columns of d
+  if (!make_map(&tmQ, BF16, p->q, qdims, qstr, qbox) || !make_map(&tmO, BF16, p->o, qdims, ostr, obox) ||
+      !make_map(&tmK, BF16, p->k, kdims, kstr, kbox) || !make_map(&tmV, BF16, p->v, kdims, vstr, vbox)) {
+    return FA2_ERR_TMA_ENCODE;
+  }
+  fa2::KArgs ka{};
+  ka.n_q = p->seqlen_q;
+  ka.n_kv = p->seqlen_kv;
+  ka.group = group;
+  ka.pack = pack;
+  ka.pack_shift = 0;
+  while ((1 << ka.pack_shift) < pack) ++ka.pack_shift;
+  ka.hblocks = p->heads_q / pack;
+  ka.bottom_right = (p->causal && p->causal_align == FA2_CAUSAL_BOTTOM_RIGHT) ? 1 : 0;
+  ka.causal_off = ka.bottom_right ? p->seqlen_kv - p->seqlen_q : 0;
+  ka.o = p->o;
+  ka.oh = p->o_stride[1];
+  ka.on = p->o_stride[2];
+  ka.d_real = p->head_dim;
+  ka.qk_scale = p->qk_scale;
+  ka.err = p->err_flag;
+  ka.gate = p->gate;
+  ka.timeout = p->timeout_cycles > 0 ? p->timeout_cycles : fa2::DEFAULT_TIMEOUT;
+  ka.num_splits = 1;
+  const int64_t rows = static_cast<int64_t>(p->seqlen_q) * pack;
+  const int64_t xblocks = static_cast<int64_t>(p->batch) * ka.hblocks;
+  const int64_t mblocks = (rows + 511) / 512;
+  const int64_t units = xblocks * mblocks;
+  if (units > 0x7fffffffLL) return FA2_ERR_SHAPE;
+  ka.xblocks = static_cast<int>(xblocks);
+  ka.div_xblocks = fa2::make_fastdiv(static_cast<uint32_t>(xblocks));
+  ka.div_hblocks = fa2::make_fastdiv(static_cast<uint32_t>(ka.hblocks));
+  ka.div_group = fa2::make_fastdiv(static_cast<uint32_t>(group));
+  ka.div_mblocks = fa2::make_fastdiv(static_cast<uint32_t>(mblocks));
+  ka.mblocks = static_cast<int>(mblocks);
+  ka.persistent = 1;
+  ka.num_units = static_cast<int>(units);
+  const int64_t clusters = units < max_clusters[device] ? units : max_clusters[device];
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+  if (cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, ka) != cudaSuccess) return FA2_ERR_LAUNCH;
+  return FA2_OK;
+}
+#endif  // FA2_PAIR
+
 template <int D, bool CAUSAL, bool BF16>
 int launch(const Fa2FwdParams* p, cudaStream_t stream, int device) {
   const bool split = plan_splits(p).num_splits > 1;
+#if FA2_PAIR != 0
+  if constexpr (D == 128) {
+    const int64_t pair_rows = static_cast<int64_t>(p->seqlen_q) * (p->pack_gqa ? p->heads_q / p->heads_kv : 1);
+    if (!split && p->cu_seqlens_q == nullptr && p->block_table == nullptr && p->head_dim == 128 &&
+        pair_rows >= FA2_PAIR_MIN_ROWS) {
+      return launch_pair<CAUSAL, BF16>(p, stream, device);
+    }
+  }
+#endif
   // Per-sequence lengths (variable-length batch or paged K/V) take the VARLEN instantiation;
   // split-KV comes with fixed lengths or paged K/V (not with cu_seqlens; validated).
   const bool per_seq = p->cu_seqlens_q != nullptr || p->block_table != nullptr;

@@ -386,4 +386,5 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
+
 }  // namespace fa2

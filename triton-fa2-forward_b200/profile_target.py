@@ -30,6 +30,7 @@ CONFIGS = {
     "full_long_bf16": (2, 32, 32, 16384, 64, torch.bfloat16, False, 0.5),
     "mha_causal_d64": (4, 16, 16, 4096, 64, torch.bfloat16, True, 1.0),
     "mqa_causal": (2, 32, 1, 4096, 128, torch.bfloat16, True, 1.0),
+    "noncausal_128": (2, 32, 8, 8192, 128, torch.bfloat16, False, 1.0),
 }
 
 
