@@ -4,6 +4,7 @@ Mirrors the role of the reference's bench/profile_target.py.
 
     python triton-fa2-forward_b200/profile_target.py [--config headline] [--warmup 2] [--launches 1]
         [--lib path/to/libfa2_sm100_variant.so]   (a library built by ablation.py)
+        [--impl fa4]   (the same shapes through vLLM's CuTe-DSL sm_100 forward, a same-box yardstick)
 
 Configs are the BASELINE.json shapes; inputs are seeded N(0,1) generated on the device.
 The headline config holds 470 MB (inputs 335 MB > 126 MB L2), so DRAM counters are meaningful.
@@ -41,7 +42,12 @@ def main():
     ap.add_argument("--launches", type=int, default=1)
     ap.add_argument("--pack", choices=["auto", "on", "off"], default="auto")
     ap.add_argument("--lib", default=None, help="load this build of libfa2_sm100.so instead of the shipped one")
+    ap.add_argument("--impl", choices=["fa2", "fa4"], default="fa2",
+                    help="fa4: vLLM's CuTe-DSL FlashAttention forward on the same shapes (yardstick)")
     args = ap.parse_args()
+    if args.impl == "fa4":
+        run_fa4(args)
+        return
     if args.lib:
         from fa2 import _lib
         _lib.LIB_PATH = os.path.abspath(args.lib)
@@ -58,6 +64,22 @@ def main():
     torch.cuda.synchronize()
     check_device_errors()
     print(f"ok: {args.config} x{args.warmup + args.launches}")
+
+
+def run_fa4(args):
+    """The same seeded shapes through vLLM's FlashAttention-4 forward ([B, N, H, D] layout), for
+    counter comparisons under a profiler. Library code, not part of this package's path."""
+    from vllm.vllm_flash_attn.cute.interface import flash_attn_func
+    B, Hq, Hkv, N, D, dt, causal, scale = CONFIGS[args.config]
+    n_q, n_kv = N if isinstance(N, tuple) else (N, N)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = (torch.randn(B, Hq, n_q, D, device="cuda", dtype=dt, generator=g) * scale).transpose(1, 2).contiguous()
+    k = (torch.randn(B, Hkv, n_kv, D, device="cuda", dtype=dt, generator=g) * scale).transpose(1, 2).contiguous()
+    v = (torch.randn(B, Hkv, n_kv, D, device="cuda", dtype=dt, generator=g) * scale).transpose(1, 2).contiguous()
+    for _ in range(args.warmup + args.launches):
+        flash_attn_func(q, k, v, causal=causal)
+    torch.cuda.synchronize()
+    print(f"ok: fa4 {args.config} x{args.warmup + args.launches}")
 
 
 if __name__ == "__main__":
