@@ -48,6 +48,9 @@ Every variant computes the full attention (no work is skipped); they differ only
   ffma_pass      s * qk_scale - m for the whole row in one FMA pass before the exponentials
                  (FA2_FFMA_PASS=1) instead of fused into the per-chunk loop
   seq_exp_ffma_pass   both
+  probe8         mbarrier waits probe 8 times per loop iteration in one PTX block (FA2_WAIT_UNROLL=8)
+  wait_suspend_20us   mbarrier waits with a 20 us suspend-time hint (FA2_WAIT_SUSPEND_NS=20000)
+                 instead of the default, as CUTLASS's barriers use (with 10 ms)
   pair           CTA pairs at D=128 (FA2_PAIR=1: fixed-length launches without split-KV of at
                  least 1024 packed rows per head block run fa2_fwd_pair_kernel, one M = 256
                  cta_group::2 MMA over two SMs with K/V split between them) instead of one CTA
@@ -116,6 +119,8 @@ COMPILED = {
     "ffma_pass": ["-DFA2_FFMA_PASS=1"],
     "seq_exp_ffma_pass": ["-DFA2_SEQ_EXP=1", "-DFA2_FFMA_PASS=1"],
     "pair": ["-DFA2_PAIR=1"],
+    "probe8": ["-DFA2_WAIT_UNROLL=8"],
+    "wait_suspend_20us": ["-DFA2_WAIT_SUSPEND_NS=20000"],
 }
 RUNTIME = {
     # name: (library variant, config it applies to, attention() keyword arguments)
