@@ -48,6 +48,8 @@ Every variant computes the full attention (no work is skipped); they differ only
   ffma_pass      s * qk_scale - m for the whole row in one FMA pass before the exponentials
                  (FA2_FFMA_PASS=1) instead of fused into the per-chunk loop
   seq_exp_ffma_pass   both
+  lane_waits     at D=128 each softmax lane runs its own probe loop for S and O and the warp votes
+                 once at the end (FA2_WARP_WAIT_D128=0) instead of warp-voted probes
   probe8         mbarrier waits probe 8 times per loop iteration in one PTX block (FA2_WAIT_UNROLL=8)
   wait_suspend_20us   mbarrier waits with a 20 us suspend-time hint (FA2_WAIT_SUSPEND_NS=20000)
                  instead of the default, as CUTLASS's barriers use (with 10 ms)
@@ -120,6 +122,7 @@ COMPILED = {
     "seq_exp_ffma_pass": ["-DFA2_SEQ_EXP=1", "-DFA2_FFMA_PASS=1"],
     "pair": ["-DFA2_PAIR=1"],
     "probe8": ["-DFA2_WAIT_UNROLL=8"],
+    "lane_waits": ["-DFA2_WARP_WAIT_D128=0"],
     "wait_suspend_20us": ["-DFA2_WAIT_SUSPEND_NS=20000"],
 }
 RUNTIME = {

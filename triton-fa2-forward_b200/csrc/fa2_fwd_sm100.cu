@@ -213,6 +213,13 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_PAIR_MIN_ROWS
 #define FA2_PAIR_MIN_ROWS 1024
 #endif
+#ifndef FA2_WARP_WAIT_D128
+// 1 (shipped): at D = 128 the softmax warps wait for S and O with warp-voted probes
+// (mbar_wait_warp: uniform branches instead of a per-lane probe loop and one vote at the end).
+// Same-box A/B, two runs: headline +0.2/+0.5%, mha_causal 0/+1.1%, pack_tail +0.6/+0.6%; at
+// D = 64 (full_long) -0.9/-2.0%, so the D = 64 build keeps the per-lane loop.
+#define FA2_WARP_WAIT_D128 1
+#endif
 #ifndef FA2_HEAD_MAJOR
 // 1: without a causal mask the persistent CTAs walk the units (batch, head) slice by slice;
 // 0: row block by row block, as with a causal mask (every head's K/V in flight at once).
@@ -1131,6 +1138,15 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
     const uint32_t tO = tmem + lane_addr + C::TMEM_O + t * D;
     const float qk_scale = a.qk_scale;
     const uint64_t sc2 = f2_pack(qk_scale, qk_scale);
+    // A whole warp's wait for S or O: true in every lane when the phase completed.
+    auto softmax_wait = [&](uint32_t b, uint32_t parity) -> bool {
+      if constexpr (D == 128 && FA2_WARP_WAIT_D128 != 0) {
+        return mbar_wait_warp(b, parity, a.timeout, a.err);
+      } else {
+        const bool w = mbar_wait(b, parity, a.timeout, a.err);
+        return __all_sync(0xffffffffu, w);
+      }
+    };
     constexpr int RCOLS = D / HALVES;  // O columns this warp rescales
     constexpr bool ALL_EPI = (C::EPI_WARPS == SOFTMAX_WARPS);
     const bool epi = ALL_EPI || h == 0;             // this warp writes O columns [epi_c0, + EPI_COLS)
@@ -1182,8 +1198,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       (void)em;
       const int e_row0 = eu.row0 + (dual ? 0 : t * BM);
       {
-        bool w = mbar_wait(bar(C::B_O_FULL + t), static_cast<uint32_t>(en) & 1u, a.timeout, a.err);
-        if (!__all_sync(0xffffffffu, w)) return false;
+        if (!softmax_wait(bar(C::B_O_FULL + t), static_cast<uint32_t>(en) & 1u)) return false;
       }
       tc_fence_after();
       constexpr int EC = C::EPI_COLS / 32;  // 32-column chunks of O this warp writes
@@ -1318,8 +1333,10 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       float m_use = -INFINITY;  // reference max of this row (scaled, base 2), the same in both warps of a pair
       float l = 0.0f;           // row sum over this warp's scores
       for (int j = 0; j < J; ++j) {
-        bool w = mbar_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(g + j) & 1u, a.timeout, a.err);
-        if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+        if (!softmax_wait(bar(C::B_S_FULL + t), static_cast<uint32_t>(g + j) & 1u)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const int col0 = (kv_base + j) * BN;
         const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0 + u.coff);

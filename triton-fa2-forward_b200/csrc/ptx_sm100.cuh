@@ -132,6 +132,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long lo
   }
 }
 
+// As mbar_wait for a whole warp (all 32 lanes call it): every probe and every exit test is a
+// warp vote, so the loop's branches are warp-uniform. Returns the same value in every lane.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, long long timeout_cycles,
+                                               const int* err) {
+  if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    if ((it & 63u) == 0u) {
+      const bool stop = (clock64() - t0 > timeout_cycles) ||
+                        (err != nullptr && *reinterpret_cast<const volatile int*>(err) != 0);
+      if (__any_sync(0xffffffffu, stop)) return false;
+    }
+  }
+}
+
 // Waits until the device word *flag becomes non-zero (written by another kernel or the
 // host), bounded like mbar_wait.
 __device__ __forceinline__ bool flag_wait(const int* flag, long long timeout_cycles, const int* err) {
