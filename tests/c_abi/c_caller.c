@@ -52,6 +52,10 @@ int main(void) {
 
   fill(&p, 2, 32, 8, 8192, 8192, 96);
   CHECK(fa2_fwd_sm100_check(&p) == FA2_ERR_HEAD_DIM, "head_dim 96 is rejected");
+  fill(&p, 2, 32, 8, 1000, 1000, 32);
+  CHECK(fa2_fwd_sm100_check(&p) == FA2_OK, "head_dim 32 runs in place on the 64 build");
+  fill(&p, 2, 32, 8, 1000, 1000, 16);
+  CHECK(fa2_fwd_sm100_check(&p) == FA2_OK, "head_dim 16 runs in place on the 64 build");
   fill(&p, 2, 30, 8, 8192, 8192, 128);
   CHECK(fa2_fwd_sm100_check(&p) == FA2_ERR_GQA, "H_q % H_kv != 0 is rejected");
   fill(&p, 2, 32, 8, 100, 200, 128);
