@@ -38,3 +38,27 @@ def test_launch_summary(tmp_path):
     first = out.splitlines()[1]
     assert "fa2_fwd_kernel" in first and first.split()[0] == "2"
     assert "96.4" in first  # 1900 us of 1970 us
+
+
+def test_step_trace_summary_reads_stamps():
+    """step_trace.summarize turns FA2_TRACE stamps into per-event medians relative to each tile's
+    S being seen (synthetic stamps: a 1000-cycle step, events at fixed offsets)."""
+    import numpy as np
+
+    import step_trace
+
+    buf = np.zeros((step_trace.UNITS, step_trace.STEPS, 2, step_trace.EVENTS), dtype=np.int64)
+    for j in range(20):
+        for t in range(2):
+            base = 10_000 + 1000 * j + 400 * t
+            for e, off in {0: 0, 1: 50, 2: 150, 3: 500, 4: 700, 5: 800, 7: 560, 8: 700, 9: 760, 10: 800,
+                           11: 820, 12: 900}.items():
+                buf[0, j, t, e] = base + off
+            for q in range(4):
+                buf[0, j, t, 20 + q] = base + 500 + 10 * q
+                buf[0, j, t, 24 + q] = base + 700 + 10 * q
+            buf[0, j, 0, 6] = 10_000 + 1000 * j + 300
+    text = step_trace.summarize(buf, 0)
+    assert "20 K/V steps" in text and "median 1000 cycles" in text
+    assert "first P hand-off" in text and "q3: 530 / 730" in text
+    assert "tile 1 S seen - tile 0 S seen: 400 cycles" in text

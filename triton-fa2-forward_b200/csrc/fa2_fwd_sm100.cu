@@ -213,6 +213,10 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #ifndef FA2_PAIR_MIN_ROWS
 #define FA2_PAIR_MIN_ROWS 1024
 #endif
+#ifndef FA2_TRACE
+// 1: compile the step-timing stamps (see FA2_STAMP); 0 (shipped): none.
+#define FA2_TRACE 0
+#endif
 #ifndef FA2_WARP_WAIT_D128
 // 1 (shipped): at D = 128 the softmax warps wait for S and O with warp-voted probes
 // (mbar_wait_warp: uniform branches instead of a per-lane probe loop and one vote at the end).
@@ -653,6 +657,25 @@ __device__ __forceinline__ bool warp_wait_pv(uint32_t bar, uint32_t parity, cons
   return __all_sync(0xffffffffu, w);
 }
 
+// Step timing (FA2_TRACE=1 builds only; triton-fa2-forward_b200/step_trace.py reads it): SM-clock
+// stamps of CTA 0's first FA2_TRACE_UNITS units, per K/V step j and Q tile t, at the hand-off points
+// of the softmax warps (warp q == 0 of each tile; per-warp copies at 16 + q ...) and the MMA thread.
+// A stamp is a clock64 read and one global store; nothing is skipped or reordered.
+#if FA2_TRACE
+#define FA2_TRACE_UNITS 4
+#define FA2_TRACE_STEPS 80
+__device__ long long g_fa2_trace[FA2_TRACE_UNITS][FA2_TRACE_STEPS][2][32];
+#define FA2_STAMP(n_, j_, t_, e_)                                                           \
+  do {                                                                                      \
+    if (blockIdx.x == 0 && (n_) < FA2_TRACE_UNITS && (j_) < FA2_TRACE_STEPS)                \
+      g_fa2_trace[(n_)][(j_)][(t_)][(e_)] = clock64();                                      \
+  } while (0)
+#else
+#define FA2_STAMP(n_, j_, t_, e_) \
+  do {                            \
+  } while (0)
+#endif
+
 // ------------------------------------------------------------------------ kernel
 // SPLIT: the split-KV build (num_splits > 1); VARLEN: the variable-length build
 // (cu_seqlens given). The host launches each exactly then; never both.
@@ -886,13 +909,18 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
       };
       // PV of tile t in two parts: the k-steps reading each softmax warp's first P_SPLIT_W
       // 32-score chunks, which the warps hand over before computing the rest, then the others.
+      [[maybe_unused]] int tr_n = 0, tr_j = 0;  // unit and step of the stamps (FA2_TRACE)
       auto pv_tile = [&](int t, int st, bool acc, uint32_t pph) -> bool {
         if (!mwait(C::B_P_FULL + t, pph)) return false;
+        FA2_STAMP(tr_n, tr_j, t, 7);
         tc_fence_after();
         issue_pv(t, st, acc, 0, 2 * P_SPLIT_W);
+        FA2_STAMP(tr_n, tr_j, t, 8);
         if (!mwait(C::B_P_LATE + t, pph)) return false;
+        FA2_STAMP(tr_n, tr_j, t, 9);
         tc_fence_after();
         issue_pv(t, st, acc, 2 * P_SPLIT_W, SCOLS / 16);
+        FA2_STAMP(tr_n, tr_j, t, 10);
         return true;
       };
       auto kv_wait = [&](int i) -> bool {
@@ -1085,16 +1113,25 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
               // previous unit's O_t (they do so during this unit's first step).
               const bool o_wait = C::DEFER && j == 0 && n > 0;
               const uint32_t oph = static_cast<uint32_t>(n - 1) & 1u;
-              if (!kv_wait(iv) || (o_wait && !mwait(C::B_O_EMPTY + 0, oph)) || !pv_tile(0, sv, j > 0, pph)) {
+              tr_n = n;
+              tr_j = j;
+              if (!kv_wait(iv)) {
+                ok = false;
+                break;
+              }
+              FA2_STAMP(n, j, 0, 6);
+              if ((o_wait && !mwait(C::B_O_EMPTY + 0, oph)) || !pv_tile(0, sv, j > 0, pph)) {
                 ok = false;
                 break;
               }
               if (last) mma_commit(bar(C::B_O_FULL + 0));
               if (more) {
                 if ((last && !mwait(C::B_Q + 0, qph_next)) || !kv_wait(ik)) { ok = false; break; }
+                FA2_STAMP(n, j, 0, 11);
                 tc_fence_after();
                 issue_qk(0, sk);
                 mma_commit(bar(C::B_S_FULL + 0));
+                FA2_STAMP(n, j, 0, 12);
                 if (qk_final) mma_commit(bar(C::B_Q_EMPTY + 0));
               }
               if ((o_wait && !mwait(C::B_O_EMPTY + 1, oph)) || !pv_tile(1, sv, j > 0, pph)) { ok = false; break; }
@@ -1102,9 +1139,11 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
               if (last) mma_commit(bar(C::B_O_FULL + 1));
               if (more) {
                 if (last && !mwait(C::B_Q + 1, qph_next)) { ok = false; break; }
+                FA2_STAMP(n, j, 1, 11);
                 tc_fence_after();
                 issue_qk(1, sk);
                 mma_commit(bar(C::B_S_FULL + 1));
+                FA2_STAMP(n, j, 1, 12);
                 mma_commit(bar(C::B_KV_EMPTY + sk));
                 if (qk_final) mma_commit(bar(C::B_Q_EMPTY + 1));
               }
@@ -1337,6 +1376,10 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           ok = false;
           break;
         }
+        if (lane == 0) {
+          if (q == 0) FA2_STAMP(n, j, t, 0);
+          FA2_STAMP(n, j, t, 16 + q);
+        }
         tc_fence_after();
         const int col0 = (kv_base + j) * BN;
         const bool need_causal = CAUSAL && (col0 + BN - 1 > tile_pos0 + u.coff);
@@ -1359,6 +1402,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < NCH; ++c) reg_fence32(s[c]);
+        if (lane == 0 && q == 0) FA2_STAMP(n, j, t, 1);
         if constexpr (C::SEP_P) {
           // S_t is in registers: the MMA warp may compute the next S_t over it.
           tc_fence_before();
@@ -1379,6 +1423,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           // P with the current reference max while the row max is taken (the two are independent
           // and use different pipes); the threshold test then runs before the hand-off.
           float m_cand = row_max_chunks(s) * qk_scale;
+          if (lane == 0 && q == 0) FA2_STAMP(n, j, t, 2);
           uint64_t nm2 = f2_pack(-m_use, -m_use);
           uint64_t acc2[4];
           float alpha = 1.0f;
@@ -1415,6 +1460,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(bar(C::B_P_FULL + t));
+          if (lane == 0) { if (q == 0) FA2_STAMP(n, j, t, 3); FA2_STAMP(n, j, t, 20 + q); }
 #pragma unroll
           for (int c = P_SPLIT_W; c < NCH; ++c) {
             uint32_t pk[16];
@@ -1424,10 +1470,12 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(bar(C::B_P_LATE + t));
+          if (lane == 0) { if (q == 0) FA2_STAMP(n, j, t, 4); FA2_STAMP(n, j, t, 24 + q); }
           seq_done();
           const uint64_t acc01 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
           float sl0, sl1;
           f2_unpack(acc01, sl0, sl1);
+          if (lane == 0 && q == 0) FA2_STAMP(n, j, t, 5);
           l = l * alpha + (sl0 + sl1);
           if (C::DEFER && pending && j == 0) {  // (not reached: the speculative path needs j > 0)
             if (!epilogue(pend, pend_n, pend_l, 0.0f)) { ok = false; break; }
@@ -1440,6 +1488,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
           for (int c = 0; c < NCH; ++c) mask_chunk(s[c], h * SCOLS + c * 32, lim);
         }
         float m_cand = row_max_chunks(s) * qk_scale;
+        if (lane == 0 && q == 0) FA2_STAMP(n, j, t, 2);
         if constexpr (HALVES == 2) {
           float m_other;
           if (!exchange(tS, tS_other, m_cand, m_other)) { ok = false; break; }
@@ -1489,11 +1538,13 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar(C::B_P_FULL + t));
+            if (lane == 0) { if (q == 0) FA2_STAMP(n, j, t, 3); FA2_STAMP(n, j, t, 20 + q); }
           }
         }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(bar(C::B_P_LATE + t));
+        if (lane == 0) { if (q == 0) FA2_STAMP(n, j, t, 4); FA2_STAMP(n, j, t, 24 + q); }
         seq_done();
 
         // Row sum of the fp32 p (before rounding, as fa2/kernel.py:98), off the critical path.
@@ -1509,6 +1560,7 @@ fa2_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ 
         const uint64_t acc01 = f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3]));
         float sl0, sl1;
         f2_unpack(acc01, sl0, sl1);
+        if (lane == 0 && q == 0) FA2_STAMP(n, j, t, 5);
         l = l * alpha + (sl0 + sl1);
         if (C::DEFER && pending && j == 0) {
           // The previous unit's output, in the gap before this unit's S_t(1) (or the next unit).
@@ -1970,6 +2022,18 @@ bool layout_ok(const int64_t st[4], const int64_t ext[4]) {
 extern "C" {
 
 int fa2_sm100_abi_version(void) { return FA2_SM100_ABI_VERSION; }
+
+#if FA2_TRACE
+// Step-timing builds only (FA2_TRACE=1): copy out / clear the stamps of the last launch.
+__attribute__((visibility("default"))) int fa2_trace_read(void* dst, int64_t bytes) {
+  if (bytes > static_cast<int64_t>(sizeof(fa2::g_fa2_trace))) bytes = sizeof(fa2::g_fa2_trace);
+  return cudaMemcpyFromSymbol(dst, fa2::g_fa2_trace, static_cast<size_t>(bytes)) == cudaSuccess ? 0 : 1;
+}
+__attribute__((visibility("default"))) int fa2_trace_clear(void) {
+  static const long long zero[sizeof(fa2::g_fa2_trace) / sizeof(long long)] = {};
+  return cudaMemcpyToSymbol(fa2::g_fa2_trace, zero, sizeof(fa2::g_fa2_trace)) == cudaSuccess ? 0 : 1;
+}
+#endif
 
 
 int64_t fa2_sm100_params_size(void) { return static_cast<int64_t>(sizeof(Fa2FwdParams)); }
