@@ -156,7 +156,9 @@ constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 #endif
 #ifndef FA2_STAGES_D128
 // K/V ring slots of 32 KiB at D = 128 (the split-KV build uses 4). A 4th slot fits only with
-// one O staging chunk per warp and measured 1-2% slower (headline, three boxes); 2 is 3% slower.
+// one O staging chunk per warp (FA2_STG_FULL 0): measured 1-2% slower on the headline with an
+// earlier build; with the current kernel, two boxes, two runs each: headline -0.2..+0.2%,
+// pack_tail +0.7..1.9%, mha_causal 0..+0.4%, MQA 0, non-causal D = 128 -0.5..-0.7%. 2 is 3% slower.
 #define FA2_STAGES_D128 3
 #endif
 #ifndef FA2_STAGES_D64
