@@ -6,17 +6,17 @@ Every variant computes the full attention (no work is skipped); they differ only
   shipped        the library as built by build.py
   no_persistent  one CTA per 256-row work unit (FA2_PERSISTENT=0) instead of one CTA per SM
                  walking the units
-  all_mufu       every exp2 on the MUFU (shipped: 25% on the FMA pipe at D=128; at D=64 12.5%
+  all_mufu       every exp2 on the MUFU (shipped: 12.5%, pairs 7 and 15, on the FMA pipe at D=128; at D=64 12.5%
                  for bf16 and none for fp16)
   emu_25         25% of the exp2 (pairs 3, 7, 11, 15) on the FMA pipe at both head dims
   emu_50         half of the exp2 on the FMA pipe at both head dims
-  emu_25_pairs_0/1/2   25% at D=128 on pairs 0,4,8,12 / 1,5,9,13 / 2,6,10,14 of each chunk
-                 (shipped: 3, 7, 11, 15)
+  emu_25_pairs_0/1/2/3   25% at D=128 on pairs 0,4,8,12 / 1,5,9,13 / 2,6,10,14 / 3,7,11,15 of
+                 each chunk (the last shipped before the warp-voted waits; shipped: 7, 15)
   d64_fp16_all_mufu   every exp2 on the MUFU at D=64 fp16 (shipped: pairs 7, 15 on the FMA pipe)
   d64_emu_pairs_3_11, d64_emu_3pairs   at D=64, pairs 3, 11 (12.5%) or 5, 10, 15 (18.75%) on the
                  FMA pipe instead of 7, 15
   d64_bf16_all_mufu   every exp2 on the MUFU at D=64 bf16
-  emu_12, emu_12_pairs_7, emu_37   12.5% (pairs 1,9 / 7,15) or 37.5% on the FMA pipe at D=128
+  emu_12, emu_37 12.5% on pairs 1, 9 or 37.5% on the FMA pipe at D=128 (emu_12_pairs_7 = shipped)
   p_split_2      P handed to the MMA warp after 64 of 128 columns (FA2_P_SPLIT=2) instead of 96
   no_spec_max    the row max taken before any exp2 at both head dims (shipped: at D=128 only)
   spec_max       P's first chunks computed with the current reference max while the row max is
@@ -90,6 +90,7 @@ COMPILED = {
     "emu_25_pairs_0": ["-DFA2_EMU_MASK_D128=0x1111u"],
     "emu_25_pairs_1": ["-DFA2_EMU_MASK_D128=0x2222u"],
     "emu_25_pairs_2": ["-DFA2_EMU_MASK_D128=0x4444u"],
+    "emu_25_pairs_3": ["-DFA2_EMU_MASK_D128=0x8888u"],
     "emu_12": ["-DFA2_EMU_MASK_D128=0x0202u"],
     "emu_12_pairs_7": ["-DFA2_EMU_MASK_D128=0x8080u"],
     "d64_fp16_all_mufu": ["-DFA2_EMU_MASK_D64=0x0u"],

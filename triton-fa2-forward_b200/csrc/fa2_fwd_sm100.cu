@@ -118,17 +118,19 @@ __host__ __device__ constexpr int s_load_x() {
 constexpr float RESCALE_TH = FA2_RESCALE_TH;     // log2 units: P may reach 2^8 before a rescale
 constexpr long long DEFAULT_TIMEOUT = 2000000000LL;  // SM clocks, ~1 s
 // Which of the 16 exp2 pairs of a 32-column chunk run on the FMA pipe (the rest on the MUFU).
-// D = 128: pairs 3, 7, 11, 15, i.e. 25% on the FMA pipe (the same share on pairs 1, 5, 9, 13
-// measured 1.4% slower on two boxes; 37.5% is 6% slower). D = 64 has half the tensor work per
-// score and less pipe headroom for the polynomial: pairs 7 and 15 (12.5%) on the FMA pipe, for
-// bf16 (degree-3 polynomial, +7% over all-MUFU) and fp16 (degree 4, +5%); 25% is slower for both.
+// D = 128: pairs 7 and 15, i.e. 12.5% on the FMA pipe. With the warp-voted softmax waits this
+// measured +0.5..0.6% (headline), +0.8% (mha_causal), +1.4..1.8% (pack_tail) over pairs 3, 7, 11,
+// 15 (25%, shipped before; the share FA4 also uses is 12.5%); 3 pairs (18.75%) were in between
+// and 37.5% is 6% slower. D = 64 has half the tensor work per score and less pipe headroom for the
+// polynomial: pairs 7 and 15 (12.5%) on the FMA pipe, for bf16 (degree-3 polynomial, +7% over
+// all-MUFU) and fp16 (+5%); 25% is slower for both.
 #ifndef FA2_POLY_DEG_FP16
 // Degree of the FMA-pipe exp2 polynomial when P is rounded to fp16. Degree 3 (max rel. error
 // 7.5e-5, below half an fp16 ulp, 2^-11 = 4.9e-4) measured +2.6% at D = 64 over degree 4 (2.7e-6).
 #define FA2_POLY_DEG_FP16 3
 #endif
 #ifndef FA2_EMU_MASK_D128
-#define FA2_EMU_MASK_D128 0x8888u
+#define FA2_EMU_MASK_D128 0x8080u
 #endif
 #ifndef FA2_EMU_MASK_D64
 #define FA2_EMU_MASK_D64 0x8080u
