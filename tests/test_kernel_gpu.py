@@ -355,17 +355,19 @@ def test_golden_fixture(path):
 
 
 # ------------------------------------------------------------------ failure detection
-def test_start_gate_timeout_is_reported():
+@pytest.mark.parametrize("D", [64, 128])
+def test_start_gate_timeout_is_reported(D):
     """A start gate that nothing opens: the kernel's bounded wait expires, it writes
     FA2_ERR_TIMEOUT to the error word, returns without a fault, and the context stays
-    usable (a normal launch right after is correct)."""
-    q, k, v = make_cuda_qkv(1, 2, 2, 256, 256, 64, torch.float16)
+    usable (a normal launch right after is correct). D = 128 runs the softmax warps'
+    warp-voted waits, D = 64 the per-lane ones."""
+    q, k, v = make_cuda_qkv(1, 2, 2, 256, 256, D, torch.float16)
     out = torch.zeros_like(q)
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     gate = torch.zeros(1, dtype=torch.int32, device="cuda")  # never set
     p = _lib.make_params(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                          q.stride(), k.stride(), v.stride(), out.stride(),
-                         1, 2, 2, 256, 256, 64, _lib.FA2_DTYPE_FP16, 1, 0, 1.4426950408889634 / 8.0,
+                         1, 2, 2, 256, 256, D, _lib.FA2_DTYPE_FP16, 1, 0, 1.4426950408889634 / D ** 0.5,
                          err_flag=err.data_ptr(), timeout_cycles=20_000_000, gate=gate.data_ptr())
     assert _lib.launch(p, torch.cuda.current_stream().cuda_stream) == _lib.FA2_OK
     torch.cuda.synchronize()
